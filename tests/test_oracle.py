@@ -1,0 +1,150 @@
+"""The oracle pinned before it is trusted (CPU only).
+
+The oracle (oracle/oracle.c) restates Siliconed's CPU arithmetic.  Here it is checked against the
+golden fixtures of tests/golden/, whose expected values come from independent implementations
+(numpy IEEE fp32, ml_dtypes e4m3fn / bf16, numpy fp64) on the reference's own test inputs:
+
+* DequantizeTests.swift:79-133   -- bit-exact ``float(q) * s`` for int8 and e4m3, every layout and scale type,
+                                    all 256 codes, counts that are not multiples of 16, a guard value past the end.
+* QuantizedMapTests.swift:132-143 -- the e4m3fn table on all 256 codes, NaN included.
+* TensorGEMMBF16.swift:43-47     -- nearest-even bf16 rounding.
+* Qwen3VLDecoderTests.swift:250-263 -- the GEMV's per-channel bar against fp64 (worst < 5e-6).
+"""
+import ctypes
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+import refgen
+from conftest import GOLDEN
+
+SCALE = {"f32": oracle.SCALE_F32, "bf16": oracle.SCALE_BF16, "f16": oracle.SCALE_F16, "none": oracle.SCALE_NONE}
+LAYOUT = {"tensor": oracle.LAYOUT_TENSOR, "columns": oracle.LAYOUT_COLUMNS, "blocks": oracle.LAYOUT_BLOCKS,
+          "rows": oracle.LAYOUT_ROWS}
+KIND = {"int8": oracle.INT8, "e4m3": oracle.E4M3}
+
+
+def canonical_sha(out: np.ndarray) -> str:
+    bits = out.view(np.uint32).copy()
+    bits[np.isnan(out)] = 0x7FC00000
+    return hashlib.sha256(bits.tobytes()).hexdigest()
+
+
+def channel_error(got: np.ndarray, exact: np.ndarray):
+    """Per-output-channel relative L2 (docs/VERIFY.md:223-232): (median, worst) over columns."""
+    d = np.linalg.norm(got.astype(np.float64) - exact, axis=0)
+    r = np.linalg.norm(exact, axis=0)
+    e = d / np.maximum(r, 1e-300)
+    return float(np.median(e)), float(e.max())
+
+
+def regenerate(case):
+    """The inputs of one DequantizeTests case, drawn in the test's own order."""
+    g = refgen.SplitMix()
+    q = g.codes(case["codes"])
+    test = case["test"]
+    if test in ("blocks", "blocks_rows"):
+        k, n, b = 100, 2052, 32
+        for st in ("f16", "bf16", "f32"):
+            sb, sv = g.scales((k + b - 1) // b * n, st)
+            if st == case["scale"]:
+                return q, sb
+    if test in ("columns", "columns_one_row"):
+        for st in ("bf16", "f32"):
+            sb, sv = g.scales(500, st)
+            if st == case["scale"]:
+                return q, sb
+    if test in ("tensor", "fp8_cast"):
+        sb, _ = g.scales(4, "f32")
+        return q, sb[:4]
+    if test == "rows":
+        sb, _ = g.scales(case["scale_count"], "bf16")
+        return q, sb
+    raise AssertionError(test)
+
+
+def test_e4m3_table_is_the_fixture():
+    ref = json.load(open(os.path.join(GOLDEN, "e4m3_table.json")))["bits"]
+    t = oracle.e4m3_table()
+    bits = t.view(np.uint32).copy()
+    bits[np.isnan(t)] = 0x7FC00000
+    assert bits.tolist() == ref
+    assert np.isnan(t[0x7F]) and np.isnan(t[0xFF]) and t[0x7E] == 448.0 and t[0x01] == 2.0 ** -9
+
+
+def test_bf16_rounding_is_nearest_even():
+    pairs = np.array(json.load(open(os.path.join(GOLDEN, "bf16_round.json")))["pairs"], np.uint64)
+    f = pairs[:, 0].astype(np.uint32).view(np.float32)
+    got = oracle.f32_to_bf16(f)
+    assert np.array_equal(got, pairs[:, 1].astype(np.uint16))
+    nan = np.array([0x7FC00001, 0xFF800001, 0x7F800001], np.uint32).view(np.float32)
+    out = oracle.f32_to_bf16(nan)
+    assert all(((int(o) & 0x7F80) == 0x7F80) and (int(o) & 0x7F) for o in out), "a NaN stays a NaN"
+
+
+@pytest.mark.parametrize("case", json.load(open(os.path.join(GOLDEN, "dequant_kats.json")))["cases"],
+                         ids=lambda c: f"{c['test']}-{c['kind']}-{c['scale']}")
+def test_dequantize_known_answers(case):
+    q, sb = regenerate(case)
+    count = case["count"]
+    out = np.full(count + 1, -7.0, np.float32)               # one guard value past the end
+    vals = np.ascontiguousarray(q[case["offset"]:])
+    s = None if case["scale"] == "none" else np.ascontiguousarray(sb)
+    L = oracle.lib()
+    L.orc_dequantize(vals.ctypes.data_as(ctypes.c_void_p), KIND[case["kind"]], count,
+                     None if s is None else s.ctypes.data_as(ctypes.c_void_p), SCALE[case["scale"]],
+                     LAYOUT[case["layout"]], case["width"], case["block"], case["first_row"],
+                     out.ctypes.data_as(ctypes.c_void_p))
+    assert out[count] == -7.0, "written past the end"
+    assert canonical_sha(out[:count]) == case["sha256"]
+    assert int(np.isnan(out[:count]).sum()) == case["nan"]
+
+
+def test_a_planted_mistake_is_caught():
+    """The comparison above is not vacuous: one value off by one ulp changes the digest."""
+    case = json.load(open(os.path.join(GOLDEN, "dequant_kats.json")))["cases"][0]
+    q, sb = regenerate(case)
+    out = oracle.dequantize(q, KIND[case["kind"]], sb, SCALE[case["scale"]], LAYOUT[case["layout"]],
+                            case["width"], case["block"], case["first_row"], count=case["count"])
+    assert canonical_sha(out) == case["sha256"]
+    bad = out.copy()
+    i = int(np.flatnonzero(np.isfinite(bad) & (bad != 0))[1000])
+    bad.view(np.uint32)[i] ^= 1
+    assert canonical_sha(bad) != case["sha256"]
+
+
+def test_gemv_splits_meet_the_reference_bar():
+    """Qwen3VLDecoderTests.swift:250-263: every scale type, 5 splits, worst channel < 5e-6 vs fp64."""
+    g = np.load(os.path.join(GOLDEN, "gemv_scale_types.npz"))
+    x = g["x"]
+    for st in ("bf16", "f16", "f32"):
+        q, sb, sv = refgen.int8_matrix(1024, 1040, 77, st)
+        if st == "f32":
+            assert hashlib.sha256(q.tobytes()).digest() == g["q_sha256"].tobytes(), "generator restatement drifted"
+        assert np.array_equal(sb, g[f"scale_bytes_{st}"])
+        rows = [oracle.gemv_int8_splits(x[r], q, sv, 5)[1] for r in range(3)]
+        med, worst = channel_error(np.stack(rows), g[f"exact_{st}"])
+        assert med < 1e-6 and worst < 5e-6, (st, med, worst)
+
+
+def test_linear_routes_against_fp64():
+    g = np.load(os.path.join(GOLDEN, "linear_small.npz"))
+    x, codes, s, b = g["int8_x"], g["int8_codes"], g["int8_s"], g["int8_bias"]
+    c, y = oracle.linear_int8(x, codes.view(np.int8), s, b)
+    med, worst = channel_error(c, g["int8_exact"])
+    assert worst < 1e-5, worst
+    assert np.array_equal(y, oracle.f32_to_bf16(c))
+    # e4m3 through the widened route: the dequantized weight is the fixture's float(q) * s, bit for bit.
+    x, codes, s, b = g["e4m3_x"], g["e4m3_codes"], g["e4m3_s"], g["e4m3_bias"]
+    k, n = codes.shape
+    w = oracle.dequantize(codes, oracle.E4M3, s, oracle.SCALE_F32, oracle.LAYOUT_COLUMNS, n).reshape(k, n)
+    assert np.array_equal(w.view(np.uint32), g["e4m3_w"].view(np.uint32))
+    c, y = oracle.linear_widened(x, w, b)
+    med, worst = channel_error(c, g["e4m3_exact"])
+    assert worst < 1e-5, worst
+    c64 = oracle.linear_fp64(x, w, b)
+    assert np.allclose(c64, g["e4m3_exact"], rtol=1e-12, atol=1e-12)
