@@ -1,0 +1,319 @@
+"""Benchmark of the quantized linear stage (one JSON line on rank 0).
+
+Default workload (config 1 of the benchmark configs, the one the headline metric is quoted on):
+one int8 weight-only linear, x bf16 [4096, 3072], W int8 [3072, 3072] per-output-channel scales,
+bf16 bias, fp32 accumulation, bf16 output.  A step is one product over that batch.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg1|cfg2|gemv1|gemv4|gemv16|gemv32]
+  python bench.py --impl reference ...   # the reference's CPU path (the oracle), on the host cores
+
+With N > 1 (one process per GPU under torch.distributed.run) every rank runs its own batch of the
+workload with the weight replicated (batch sharding: the images / token batches are independent, no
+collective on the data path); ``value`` is the work of all ranks over the slowest rank's time.
+Timing: W untimed warm-up steps, then K timed steps, each bracketed by CUDA events on the launching
+stream, with the L2 flushed (a 256 MiB write) before every step; barrier + synchronize around the
+timed region; the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"]))}, "measured"
+    return dict(FALLBACK_PEAKS, bf16_tflops_sustained=1400.0), "fallback"
+
+
+def make_case(workload: str):
+    from siliconed_b200 import configs
+    if workload == "cfg1":
+        return configs.config1()
+    if workload == "cfg2":
+        return configs.config2()
+    if workload.startswith("gemv"):
+        m = int(workload[4:] or 1)
+        return configs.config4(m, 12288, 4096)
+    raise SystemExit(f"unknown workload {workload}")
+
+
+def describe(case, workload):
+    bound = "hbm" if case.m <= 32 else "tensor"
+    return {"workload": f"{workload}: {case.name} x bf16 [{case.m}, {case.k}] . W [{case.k}, {case.n}] "
+                        f"{'int8' if case.kind == 1 else 'e4m3'} per-channel, fp32 accumulate, bf16 out",
+            "m": case.m, "k": case.k, "n": case.n, "bias": case.bias is not None, "bound": bound,
+            "l2": "flushed before every timed step (256 MiB write)"}
+
+
+def metric_of(case):
+    if case.m <= 32:
+        return "int8-weight GEMV achieved HBM GB/s", "GB/s"
+    return "int8-weight GEMM TFLOP/s at M=4096" if case.kind == 1 else "fp8-weight GEMM TFLOP/s at M=4096", "TFLOP/s"
+
+
+def throughput(case, seconds, unit, ranks=1):
+    if unit == "GB/s":
+        return ranks * case.bytes_moved() / seconds / 1e9
+    return ranks * case.flops / seconds / 1e12
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, v in enumerate(flags) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(case, budget_s: float = 12.0):
+    """The reference's CPU path restated (the oracle): dequantize W (OpenMP, all host threads), then
+    an fp32 GEMM on the CPU (torch.matmul, all threads), on a bounded sample of the rows."""
+    import torch
+    import oracle
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    torch.set_num_threads(threads)
+    codes_kn = np.ascontiguousarray(case.codes_nk.T)
+    rows = case.m if case.m <= 32 else 256
+    x = torch.from_numpy(((case.x[:rows].astype(np.uint32) << 16).view(np.float32)).copy())
+    bias = None if case.bias is None else torch.from_numpy((case.bias.astype(np.uint32) << 16).view(np.float32))
+    reps, t_total = 0, 0.0
+    while t_total < budget_s and reps < 1000:
+        t0 = time.perf_counter()
+        w = oracle.dequantize(codes_kn, case.kind, case.scales, oracle.SCALE_F32, oracle.LAYOUT_COLUMNS,
+                              case.n).reshape(case.k, case.n)
+        y = x @ torch.from_numpy(w)
+        if bias is not None:
+            y += bias
+        t_total += time.perf_counter() - t0
+        reps += 1
+    per = t_total / reps
+    flops = 2.0 * rows * case.k * case.n
+    byts = rows * case.k * 2 + case.n * case.k + case.n * 4 + rows * case.n * 2
+    return per, flops, byts, threads, rows, reps
+
+
+def run_reference(args):
+    """--impl reference: the CPU path timed on this box's host cores, on the same metric."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    case = make_case(args.workload)
+    metric, unit = metric_of(case)
+    for _ in range(max(args.warmup, 0) and 1):
+        cpu_baseline(case, budget_s=0.0)
+    per, flops, byts, threads, rows, reps = cpu_baseline(case, budget_s=max(1.0, 2.0 * args.steps))
+    value = (byts / per / 1e9) if unit == "GB/s" else (flops / per / 1e12)
+    sample = (f"{rows} of {case.m} rows per step ({reps} steps timed), full weight dequantized each step "
+              f"(oracle/ C, OpenMP) + fp32 torch.matmul on the CPU")
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
+            "steps": reps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": describe(case, args.workload),
+            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from siliconed_b200.products import Context, QuantizedWeight
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    case = make_case(args.workload)
+    metric, unit = metric_of(case)
+    ctx = Context(local)
+    w = QuantizedWeight(ctx, case.codes_nk, case.kind, case.scales, published_nk=True)
+    x = torch.from_numpy(case.x.view(np.int16)).cuda().view(torch.bfloat16)
+    bias = None if case.bias is None else torch.from_numpy(case.bias.view(np.int16)).cuda().view(torch.bfloat16)
+    y = torch.empty((case.m, case.n), dtype=torch.bfloat16, device="cuda")
+    ws_bytes = w.workspace_bytes(case.m)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        w.linear(x, bias=bias, out=y, workspace=ws, stream=stream)
+
+    for _ in range(args.warmup):
+        flush.fill_(1)
+        step()
+    ctx.poll_errors()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ctx.poll_errors()
+    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]  # ms
+    t_ms = float(sum(per_step))
+    t = torch.tensor([t_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_ms = float(t.item())
+    sec_per_step = t_ms / 1e3 / args.steps
+    value = throughput(case, sec_per_step, unit, ranks=world)
+
+    # End to end through the public API with host buffers: H2D of x, the product, D2H of y, per step.
+    x_host = torch.from_numpy(case.x.view(np.int16)).view(torch.bfloat16).pin_memory()
+    y_host = torch.empty((case.m, case.n), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        x_dev.copy_(x_host, non_blocking=True)
+        w.linear(x_dev, bias=bias, out=y, workspace=ws, stream=stream)
+        y_host.copy_(y, non_blocking=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        w.linear(x_dev, bias=bias, out=y, workspace=ws, stream=stream)
+        y_host.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    e2e_value = throughput(case, float(te.item()) / 1e3 / e2e_steps, unit, ranks=world)
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        if unit == "GB/s":
+            achieved = case.bytes_moved() / sec_per_step / 1e9
+            peak, runit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
+        else:
+            achieved = case.flops / sec_per_step / 1e12
+            peak, runit, bound = peaks["bf16_tflops"], "TFLOP/s", "tensor"
+        traffic = None
+        tpath = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tpath):
+            traffic = json.load(open(tpath)).get(args.workload)
+        line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": dict(describe(case, args.workload), parallelism=f"replicas x{world} (batch-sharded)"),
+                "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": runit,
+                             "frac": achieved / peak, "traffic": traffic,
+                             "peak_source": f"{peak_src} (burst figure: the kernel is timed alone)"},
+                "clocks": clocks.summary(),
+                "e2e": {"value": e2e_value, "unit": unit,
+                        "h2d_bytes_per_step": int(case.x.nbytes),
+                        "d2h_bytes_per_step": int(case.m * case.n * 2),
+                        "path": "QuantizedWeight.linear (sc_linear) with pinned host x / y copied in the timed region"},
+                "gpu_launches": args.steps * (1 if case.m > 32 else -(-case.m // 8)),
+                "step_ms_min": min(per_step), "step_ms_median": statistics.median(per_step)}
+        if not args.no_cpu_baseline:
+            per, flops, byts, threads, rows, reps = cpu_baseline(case)
+            cv = (byts / per / 1e9) if unit == "GB/s" else (flops / per / 1e12)
+            line["cpu_baseline"] = {"value": cv, "unit": unit, "cores": threads, "kind": "port",
+                                    "sample": f"{rows} of {case.m} rows, {reps} reps: oracle dequant (C, OpenMP) "
+                                              f"+ fp32 torch.matmul, {per * 1e3:.1f} ms each"}
+        print(json.dumps(line), flush=True)
+    w.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="cfg1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,180 @@
+/*
+ * siliconed_cuda.h -- the C ABI of libsiliconed_cuda, a B200 (sm_100a) implementation of
+ * Siliconed's quantized linear stage: the int8 / fp8 (e4m3fn) weight-only
+ * dequantize-and-multiply behind every DiT and text-encoder projection.
+ *
+ * Plain C: pointers, sizes and integer status codes; no exceptions, aborts or C++ types cross it.
+ * A SwiftPM system-library target can wrap this header directly through a module map.
+ *
+ * Conventions
+ *   - Weights are given in the map's layout: q [K, N] row-major, N contiguous, one byte per value
+ *     (Sources/Siliconed/Artifact.swift:15-57, linear_weights_transposed = true), with per-output
+ *     (per-column) or per-tensor scales in fp32, bf16 or fp16.  SC_WEIGHT_PUBLISHED_NK accepts the
+ *     published nn.Linear layout [N, K] instead.
+ *   - Activations and outputs are bf16 (uint16 bit patterns), row-major: x [M, K], y [M, N].
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream).  Every compute call is
+ *     asynchronous on that stream; sc_sync / sc_poll_errors wait.
+ *   - A context is used by one host thread at a time; distinct contexts may run concurrently.
+ *   - The library never falls back to the CPU: without a usable sm_100 device every call fails.
+ */
+#ifndef SILICONED_CUDA_H
+#define SILICONED_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SC_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define SC_API __attribute__((visibility("default")))
+#else
+#define SC_API
+#endif
+
+/* Status of every call.  Replaces Swift `throws` (Artifact.Failure, WeightProducts.swift:430) and
+ * the nil-and-fallback of refused routes (TensorGEMM.swift:204-232): here a refusal is an error. */
+typedef enum sc_status {
+    SC_OK = 0,
+    SC_INVALID_ARG = 1,          /* null pointer, negative size, unknown enum value */
+    SC_UNSUPPORTED_SHAPE = 2,    /* a dimension the kernels cannot take (e.g. K not a multiple of 8) */
+    SC_UNALIGNED = 3,            /* x / y / bias not 16-byte aligned where a kernel needs it */
+    SC_CUDA_ERROR = 4,           /* a CUDA runtime call failed; see sc_last_error_string */
+    SC_TIMEOUT = 5,              /* a bounded device-side wait gave up (reported by sc_poll_errors) */
+    SC_OUT_OF_MEMORY = 6,        /* a weight's device arena could not be allocated */
+    SC_REFUSED = 7,              /* a weight the forge refuses: a scale whose products are subnormal */
+    SC_WORKSPACE_TOO_SMALL = 8,  /* the caller's workspace is smaller than sc_workspace_size */
+    SC_NO_DEVICE = 9             /* no CUDA device, or not an sm_100 part */
+} sc_status;
+
+/* 8-bit weight kinds (Artifact.DType .int8 / .float8_e4m3). */
+typedef enum sc_weight_kind { SC_WEIGHT_INT8 = 1, SC_WEIGHT_E4M3 = 2 } sc_weight_kind;
+
+/* Scale element type as published (Artifact.Scale.dtype, Artifact.swift:38-57). */
+typedef enum sc_scale_type { SC_SCALE_F32 = 1, SC_SCALE_BF16 = 2, SC_SCALE_F16 = 3 } sc_scale_type;
+
+/* Scale layout (Widen.ScaleLayout .tensor / .columns, Widen.swift:100-110). */
+typedef enum sc_scale_layout { SC_SCALE_TENSOR = 0, SC_SCALE_COLUMNS = 1 } sc_scale_layout;
+
+/* Output element type of sc_linear_ex: bf16 (the north star's) or fp32 (the reference's own C,
+ * TensorGEMM.linear(... c: MTLBuffer) writes fp32, TensorGEMM.swift:264-267). */
+typedef enum sc_out_type { SC_OUT_BF16 = 0, SC_OUT_F32 = 1 } sc_out_type;
+
+/* Flags of sc_weight_create. */
+#define SC_WEIGHT_VALUES_ON_DEVICE 0x1u /* values and scales are device pointers (else host) */
+#define SC_WEIGHT_PUBLISHED_NK 0x2u     /* values are the published [N, K] rows, not the map's [K, N] */
+
+typedef uint16_t sc_bf16;
+typedef struct sc_ctx sc_ctx;
+typedef struct sc_weight sc_weight;
+
+/* ---- context ------------------------------------------------------------------------------ */
+
+SC_API int sc_abi_version(void);
+SC_API const char* sc_status_string(sc_status status);
+
+/* Opens a context on CUDA device `device` (made current for the calling thread).  Replaces the
+ * engine's GEMM/TensorGEMM objects (GEMM.swift:168-225, TensorGEMM.swift:58-80). */
+SC_API sc_status sc_ctx_create(int device, sc_ctx** out);
+SC_API void sc_ctx_destroy(sc_ctx* ctx);
+/* The last error message of this context ("" if none); valid until the next call on it. */
+SC_API const char* sc_last_error_string(const sc_ctx* ctx);
+
+/* ---- weights ------------------------------------------------------------------------------ */
+
+/*
+ * Registers one 8-bit linear weight: values q (k*n bytes) and scales (1 or n elements of
+ * scale_type).  The library copies them once into its own device arena, re-tiled for the kernels
+ * (transposed to [N, K], values biased to unsigned for int8, K padded to 64 and N to 256, scales
+ * widened to fp32 after the values); the caller keeps ownership of its buffers.  Replaces the map
+ * tensor + Scale (Artifact.swift:15-57), Artifact.stageInt8 (Artifact.swift:755-777) and the
+ * reserve plan (WeightProducts.int8Plan, WeightProducts.swift:564-610).
+ * Refuses (SC_REFUSED) a nonzero scale whose smallest product is subnormal in fp32
+ * (QuantizedLayouts.checkSubnormal, Forge/Quantization.swift:387-403).
+ * `stream` orders the upload; the weight is usable on any stream once that stream has reached it.
+ */
+SC_API sc_status sc_weight_create(sc_ctx* ctx, const void* values, sc_weight_kind kind, int64_t k, int64_t n,
+                           const void* scales, sc_scale_type scale_type, sc_scale_layout layout, uint32_t flags,
+                           void* stream, sc_weight** out);
+
+/*
+ * The same for the columns [n_begin, n_end) of a [K, N] weight only: the shard a rank holds in a
+ * column-parallel (N-sharded) linear.  `values`/`scales` describe the whole tensor.
+ */
+SC_API sc_status sc_weight_create_shard(sc_ctx* ctx, const void* values, sc_weight_kind kind, int64_t k, int64_t n,
+                                 const void* scales, sc_scale_type scale_type, sc_scale_layout layout,
+                                 uint32_t flags, int64_t n_begin, int64_t n_end, void* stream, sc_weight** out);
+
+SC_API sc_status sc_weight_destroy(sc_ctx* ctx, sc_weight* w);
+
+/* Shape, kind and device bytes of a registered weight (any out pointer may be NULL). */
+SC_API sc_status sc_weight_info(const sc_weight* w, int64_t* k, int64_t* n, int* kind, size_t* device_bytes);
+
+/*
+ * Exports the dequantized weight, fp32 [K, N] (device pointer `out`), equal bit for bit to
+ * Widen.dequantize: float(q) * s, one rounded multiply (Artifact.materialize, Artifact.swift:670-715
+ * -> Widen.swift:129-271).
+ */
+SC_API sc_status sc_dequantize(sc_ctx* ctx, const sc_weight* w, float* out, void* stream);
+
+/* ---- products ----------------------------------------------------------------------------- */
+
+/* Scratch bytes a product of `m` rows on `w` needs (0 when it needs none).  The caller owns the
+ * workspace; the library allocates nothing on the product path (WeightProducts.swift:50-53). */
+SC_API sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* bytes);
+
+/*
+ * y[m, n] = bf16( (sum_k x[m, k] * float(q[k, n])) * s[n] + bias[n] ), fp32 accumulation, the
+ * scale applied after the sum as the native int8 route does (linear_int8 + scale_columns,
+ * TensorGEMM.swift:125-179), the bias after it (DiT.swift:410-413), nearest-even bf16
+ * (TensorGEMMBF16.swift:43-47).  bias may be NULL.  Replaces TensorGEMM.linear(a:int8:...)
+ * (TensorGEMM.swift:264-290) / submitRounded (TensorGEMMBF16.swift:208-264) and, for e4m3, the
+ * widened route (WeightProducts.swift:995-1001 -> GEMM.linear, GEMM.swift:297-345).
+ * Dispatches on the weight's kind and on m: m <= 32 runs the skinny GEMV, larger m the
+ * tensor-core GEMM.  x, y, bias: device pointers, 16-byte aligned; K a multiple of 8.
+ * workspace may be NULL when sc_workspace_size reports 0.
+ */
+SC_API sc_status sc_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* sc_linear with the output type chosen: y is bf16 [m, n] (SC_OUT_BF16) or fp32 [m, n] (SC_OUT_F32,
+ * the reference's C buffer; the same sum, scale and bias, without the final rounding to bf16). */
+SC_API sc_status sc_linear_ex(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, void* y,
+                              sc_out_type y_type, void* workspace, size_t workspace_bytes, void* stream);
+
+/* sc_linear for an int8 weight (SC_INVALID_ARG on another kind). */
+SC_API sc_status sc_linear_w8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* sc_linear for an e4m3 weight (SC_INVALID_ARG on another kind). */
+SC_API sc_status sc_linear_fp8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
+                        sc_bf16* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * The skinny product for 1 <= m <= 32 rows (token decode, short encoder prompts), either weight
+ * kind: split-K over the GPU with partial sums in `workspace` added in a fixed order, so that every
+ * run gives the same bits.  Replaces DecodeKernels.gemv (DecodeKernels.swift:458-470, kernel
+ * gemv_int8 :67-109, splits :450-453).
+ */
+SC_API sc_status sc_gemv_w8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- synchronisation and device-side errors ----------------------------------------------- */
+
+/* Waits for `stream`. */
+SC_API sc_status sc_sync(sc_ctx* ctx, void* stream);
+
+/*
+ * Waits for `stream`, then reads and clears the context's device error word: SC_TIMEOUT when a
+ * bounded wait inside a kernel gave up (the kernel then released its resources and returned),
+ * SC_CUDA_ERROR on an asynchronous CUDA error, SC_OK otherwise.
+ */
+SC_API sc_status sc_poll_errors(sc_ctx* ctx, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SILICONED_CUDA_H */

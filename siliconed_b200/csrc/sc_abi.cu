@@ -1,0 +1,437 @@
+// The C ABI of libsiliconed_cuda (include/siliconed_cuda.h): argument checks, the weight arena's
+// registration, and dispatch to the kernels.  No entry point throws, traps or falls back to the CPU.
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "sc_internal.h"
+
+namespace sc {
+
+sc_status fail(sc_ctx* ctx, sc_status status, const std::string& message) {
+  if (ctx != nullptr) ctx->last_error = message;
+  return status;
+}
+
+sc_status check_cuda(sc_ctx* ctx, cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return SC_OK;
+  cudaGetLastError();  // clear a sticky launch error of this thread
+  std::string m = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+  return fail(ctx, e == cudaErrorMemoryAllocation ? SC_OUT_OF_MEMORY : SC_CUDA_ERROR, m);
+}
+
+namespace {
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// IEEE binary16 -> fp32, exact.
+float half_bits_to_f32(uint16_t h) {
+  const uint32_t sign = static_cast<uint32_t>(h & 0x8000u) << 16;
+  const int e = (h >> 10) & 0x1F, f = h & 0x3FF;
+  uint32_t bits;
+  if (e == 0x1F) {
+    bits = sign | 0x7F800000u | (static_cast<uint32_t>(f) << 13);
+  } else if (e == 0) {
+    float v = std::ldexp(static_cast<float>(f), -24);
+    std::memcpy(&bits, &v, 4);
+    bits |= sign;
+  } else {
+    bits = sign | (static_cast<uint32_t>(e - 15 + 127) << 23) | (static_cast<uint32_t>(f) << 13);
+  }
+  float out;
+  std::memcpy(&out, &bits, 4);
+  return out;
+}
+
+float scale_to_f32(const uint8_t* scales, sc_scale_type t, int64_t i) {
+  switch (t) {
+    case SC_SCALE_F32: {
+      float v;
+      std::memcpy(&v, scales + 4 * i, 4);
+      return v;
+    }
+    case SC_SCALE_BF16: {
+      uint16_t b;
+      std::memcpy(&b, scales + 2 * i, 2);
+      const uint32_t bits = static_cast<uint32_t>(b) << 16;
+      float v;
+      std::memcpy(&v, &bits, 4);
+      return v;
+    }
+    default: {
+      uint16_t h;
+      std::memcpy(&h, scales + 2 * i, 2);
+      return half_bits_to_f32(h);
+    }
+  }
+}
+
+size_t scale_size(sc_scale_type t) { return t == SC_SCALE_F32 ? 4 : 2; }
+
+bool is_device_pointer(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+sc_status enter(sc_ctx* ctx) {
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess) return check_cuda(ctx, cudaGetLastError(), "cudaGetDevice");
+  if (cur != ctx->device) return check_cuda(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  return SC_OK;
+}
+
+sc_status make_tmap_x(sc_ctx* ctx, const sc_bf16* x, int64_t m, int64_t k, CUtensorMap* map) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<sc_bf16*>(x), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, SC_CUDA_ERROR, "cuTensorMapEncodeTiled (activations) failed: " + std::to_string(r));
+  return SC_OK;
+}
+
+sc_status make_tmap_w(sc_ctx* ctx, sc_weight* w) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w->k_pad), static_cast<cuuint64_t>(w->n_pad)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w->k_pad)};
+  const cuuint32_t box[2] = {64, 256};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = ctx->encode_tiled(&w->tmap_values, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->values, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, SC_CUDA_ERROR, "cuTensorMapEncodeTiled (weights) failed: " + std::to_string(r));
+  return SC_OK;
+}
+
+sc_status check_product_args(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
+                             const void* y) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (w == nullptr || x == nullptr || y == nullptr) return fail(ctx, SC_INVALID_ARG, "null weight, x or y");
+  if (m < 0) return fail(ctx, SC_INVALID_ARG, "m < 0");
+  if (m > 0x7FFFFFFF || w->k > 0x7FFFFFFF) return fail(ctx, SC_UNSUPPORTED_SHAPE, "m or k beyond 2^31 - 1");
+  if (w->device != ctx->device) return fail(ctx, SC_INVALID_ARG, "weight registered on another device");
+  if (w->k % 8 != 0) return fail(ctx, SC_UNSUPPORTED_SHAPE, "K must be a multiple of 8 (16-byte activation rows)");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u)
+    return fail(ctx, SC_UNALIGNED, "x and y must be 16-byte aligned");
+  if (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 1u)) return fail(ctx, SC_UNALIGNED, "bias must be 2-byte aligned");
+  if (m > 0) {
+    if (!is_device_pointer(x) || !is_device_pointer(y) || (bias != nullptr && !is_device_pointer(bias)))
+      return fail(ctx, SC_INVALID_ARG, "x, y and bias must be device (or managed) memory");
+  }
+  return SC_OK;
+}
+
+sc_status run_gemv(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, void* y,
+                   bool f32_out, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  const size_t need = gemv_workspace_bytes(w, m, ctx->sm_count);
+  if (workspace_bytes < need || (need > 0 && workspace == nullptr))
+    return fail(ctx, SC_WORKSPACE_TOO_SMALL, "workspace smaller than sc_workspace_size");
+  const int splits = gemv_splits(w, m, ctx->sm_count);
+  return check_cuda(ctx, launch_gemv(w, x, m, bias, y, f32_out, static_cast<float*>(workspace), splits, st),
+                    "gemv launch");
+}
+
+sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, void* y,
+                     bool f32_out, void* workspace, size_t workspace_bytes, void* stream, int want_kind) {
+  sc_status s = check_product_args(ctx, w, x, m, bias, y);
+  if (s != SC_OK) return s;
+  if (want_kind != 0 && w->kind != want_kind)
+    return fail(ctx, SC_INVALID_ARG, want_kind == SC_WEIGHT_INT8 ? "not an int8 weight" : "not an e4m3 weight");
+  if (m == 0) return SC_OK;
+  if ((s = enter(ctx)) != SC_OK) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (m <= 32) return run_gemv(ctx, w, x, m, bias, y, f32_out, workspace, workspace_bytes, st);
+  CUtensorMap tmx;
+  if ((s = make_tmap_x(ctx, x, m, w->k, &tmx)) != SC_OK) return s;
+  return check_cuda(ctx, launch_gemm_tc(tmx, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st), "gemm launch");
+}
+
+}  // namespace
+}  // namespace sc
+
+using namespace sc;
+
+extern "C" {
+
+int sc_abi_version(void) { return SC_ABI_VERSION; }
+
+const char* sc_status_string(sc_status status) {
+  switch (status) {
+    case SC_OK: return "ok";
+    case SC_INVALID_ARG: return "invalid argument";
+    case SC_UNSUPPORTED_SHAPE: return "unsupported shape";
+    case SC_UNALIGNED: return "unaligned pointer";
+    case SC_CUDA_ERROR: return "CUDA error";
+    case SC_TIMEOUT: return "device-side wait timed out";
+    case SC_OUT_OF_MEMORY: return "out of device memory";
+    case SC_REFUSED: return "weight refused";
+    case SC_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case SC_NO_DEVICE: return "no usable sm_100 device";
+  }
+  return "unknown status";
+}
+
+sc_status sc_ctx_create(int device, sc_ctx** out) {
+  if (out == nullptr) return SC_INVALID_ARG;
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return SC_NO_DEVICE;
+  }
+  if (device < 0 || device >= count) return SC_INVALID_ARG;
+  if (cudaSetDevice(device) != cudaSuccess) {
+    cudaGetLastError();
+    return SC_NO_DEVICE;
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) {
+    cudaGetLastError();
+    return SC_NO_DEVICE;
+  }
+  sc_ctx* ctx = new (std::nothrow) sc_ctx();
+  if (ctx == nullptr) return SC_OUT_OF_MEMORY;
+  ctx->device = device;
+  ctx->sm_count = prop.multiProcessorCount;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || fn == nullptr) {
+    cudaGetLastError();
+    delete ctx;
+    return SC_NO_DEVICE;
+  }
+  ctx->encode_tiled = reinterpret_cast<sc_encode_tiled_fn>(fn);
+  if (cudaMalloc(&ctx->d_err, kErrWords * sizeof(int)) != cudaSuccess ||
+      cudaMemset(ctx->d_err, 0, kErrWords * sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    if (ctx->d_err) cudaFree(ctx->d_err);
+    delete ctx;
+    return SC_OUT_OF_MEMORY;
+  }
+  *out = ctx;
+  return SC_OK;
+}
+
+void sc_ctx_destroy(sc_ctx* ctx) {
+  if (ctx == nullptr) return;
+  int cur = -1;
+  cudaGetDevice(&cur);
+  cudaSetDevice(ctx->device);
+  if (ctx->d_err) cudaFree(ctx->d_err);
+  if (cur >= 0) cudaSetDevice(cur);
+  delete ctx;
+}
+
+const char* sc_last_error_string(const sc_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
+
+sc_status sc_weight_create_shard(sc_ctx* ctx, const void* values, sc_weight_kind kind, int64_t k, int64_t n,
+                                 const void* scales, sc_scale_type scale_type, sc_scale_layout layout, uint32_t flags,
+                                 int64_t n_begin, int64_t n_end, void* stream, sc_weight** out) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (out == nullptr || values == nullptr || scales == nullptr) return fail(ctx, SC_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (kind != SC_WEIGHT_INT8 && kind != SC_WEIGHT_E4M3) return fail(ctx, SC_INVALID_ARG, "unknown weight kind");
+  if (scale_type != SC_SCALE_F32 && scale_type != SC_SCALE_BF16 && scale_type != SC_SCALE_F16)
+    return fail(ctx, SC_INVALID_ARG, "unknown scale type");
+  if (layout != SC_SCALE_TENSOR && layout != SC_SCALE_COLUMNS) return fail(ctx, SC_INVALID_ARG, "unknown scale layout");
+  if (flags & ~(SC_WEIGHT_VALUES_ON_DEVICE | SC_WEIGHT_PUBLISHED_NK)) return fail(ctx, SC_INVALID_ARG, "unknown flags");
+  if (k <= 0 || n <= 0) return fail(ctx, SC_INVALID_ARG, "k and n must be positive");
+  if (n_begin < 0 || n_end > n || n_begin >= n_end) return fail(ctx, SC_INVALID_ARG, "bad column range");
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool on_device = (flags & SC_WEIGHT_VALUES_ON_DEVICE) != 0;
+  const bool published = (flags & SC_WEIGHT_PUBLISHED_NK) != 0;
+  const int64_t cols = n_end - n_begin;
+
+  // Scales: widened exactly to fp32, checked, padded.
+  const int64_t scount = layout == SC_SCALE_TENSOR ? 1 : n;
+  std::vector<uint8_t> sbytes(static_cast<size_t>(scount) * scale_size(scale_type));
+  if (on_device) {
+    if ((s = check_cuda(ctx, cudaMemcpy(sbytes.data(), scales, sbytes.size(), cudaMemcpyDeviceToHost), "scales to host")) != SC_OK)
+      return s;
+  } else {
+    std::memcpy(sbytes.data(), scales, sbytes.size());
+  }
+  const float smallest = kind == SC_WEIGHT_INT8 ? 1.0f : std::ldexp(1.0f, -9);
+  for (int64_t i = 0; i < scount; ++i) {
+    const float v = scale_to_f32(sbytes.data(), scale_type, i);
+    if (v != 0.0f && std::fabs(v) * smallest < FLT_MIN) {
+      char msg[160];
+      std::snprintf(msg, sizeof msg, "scale %lld = %g: its products can fall below 2^-126 (subnormal)",
+                    static_cast<long long>(i), static_cast<double>(v));
+      return fail(ctx, SC_REFUSED, msg);
+    }
+  }
+  sc_weight* w = new (std::nothrow) sc_weight();
+  if (w == nullptr) return fail(ctx, SC_OUT_OF_MEMORY, "host allocation");
+  w->kind = kind;
+  w->k = k;
+  w->n = cols;
+  w->k_pad = round_up(k, kArenaKAlign);
+  w->n_pad = round_up(cols, kArenaNAlign);
+  w->device = ctx->device;
+  std::vector<float> sf(static_cast<size_t>(w->n_pad), 0.0f);
+  for (int64_t j = 0; j < cols; ++j)
+    sf[static_cast<size_t>(j)] = scale_to_f32(sbytes.data(), scale_type, layout == SC_SCALE_TENSOR ? 0 : n_begin + j);
+
+  const size_t vbytes = static_cast<size_t>(w->n_pad * w->k_pad);
+  const size_t soff = static_cast<size_t>(round_up(static_cast<int64_t>(vbytes), 256));
+  w->bytes = soff + static_cast<size_t>(w->n_pad) * sizeof(float);
+  auto cleanup = [&](sc_status st_) {
+    if (w->arena) cudaFree(w->arena);
+    delete w;
+    return st_;
+  };
+  if ((s = check_cuda(ctx, cudaMalloc(&w->arena, w->bytes), "weight arena")) != SC_OK) return cleanup(s);
+  w->values = w->arena;
+  w->scales = reinterpret_cast<float*>(w->arena + soff);
+
+  // Source codes on the device: the caller's, or a staging copy of the needed part.
+  uint8_t* staging = nullptr;
+  int* nan_flag = nullptr;
+  const uint8_t* src = static_cast<const uint8_t*>(values);
+  int64_t src_n_total = n, src_n_begin = n_begin;
+  if (!on_device) {
+    if ((s = check_cuda(ctx, cudaMalloc(&staging, static_cast<size_t>(k * cols) + 16), "staging")) != SC_OK)
+      return cleanup(s);
+    cudaError_t e;
+    if (published)  // rows [n_begin, n_end) of [N, K] are contiguous
+      e = cudaMemcpyAsync(staging, src + n_begin * k, static_cast<size_t>(k * cols), cudaMemcpyHostToDevice, st);
+    else  // columns [n_begin, n_end) of [K, N]: a pitched copy
+      e = cudaMemcpy2DAsync(staging, static_cast<size_t>(cols), src + n_begin, static_cast<size_t>(n),
+                            static_cast<size_t>(cols), static_cast<size_t>(k), cudaMemcpyHostToDevice, st);
+    if ((s = check_cuda(ctx, e, "weight upload")) != SC_OK) {
+      cudaFree(staging);
+      return cleanup(s);
+    }
+    src = staging;
+    src_n_total = cols;
+    src_n_begin = 0;
+  }
+  cudaError_t e = cudaMalloc(&nan_flag, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemsetAsync(nan_flag, 0, sizeof(int), st);
+  if (e == cudaSuccess)
+    e = launch_retile(src, published, kind, k, src_n_total, src_n_begin, cols, w->values, w->k_pad, w->n_pad, nan_flag, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(w->scales, sf.data(), sf.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+  int nan_host = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&nan_host, nan_flag, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (staging) cudaFree(staging);
+  if (nan_flag) cudaFree(nan_flag);
+  if ((s = check_cuda(ctx, e, "weight re-tiling")) != SC_OK) return cleanup(s);
+  w->has_nan_codes = nan_host != 0;
+  if ((s = make_tmap_w(ctx, w)) != SC_OK) return cleanup(s);
+  *out = w;
+  return SC_OK;
+}
+
+sc_status sc_weight_create(sc_ctx* ctx, const void* values, sc_weight_kind kind, int64_t k, int64_t n,
+                           const void* scales, sc_scale_type scale_type, sc_scale_layout layout, uint32_t flags,
+                           void* stream, sc_weight** out) {
+  return sc_weight_create_shard(ctx, values, kind, k, n, scales, scale_type, layout, flags, 0, n, stream, out);
+}
+
+sc_status sc_weight_destroy(sc_ctx* ctx, sc_weight* w) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (w == nullptr) return SC_OK;
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != w->device) cudaSetDevice(w->device);
+  const cudaError_t e = cudaFree(w->arena);
+  if (cur >= 0 && cur != w->device) cudaSetDevice(cur);
+  delete w;
+  return check_cuda(ctx, e, "cudaFree (weight arena)");
+}
+
+sc_status sc_weight_info(const sc_weight* w, int64_t* k, int64_t* n, int* kind, size_t* device_bytes) {
+  if (w == nullptr) return SC_INVALID_ARG;
+  if (k) *k = w->k;
+  if (n) *n = w->n;
+  if (kind) *kind = w->kind;
+  if (device_bytes) *device_bytes = w->bytes;
+  return SC_OK;
+}
+
+sc_status sc_dequantize(sc_ctx* ctx, const sc_weight* w, float* out, void* stream) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (w == nullptr || out == nullptr) return fail(ctx, SC_INVALID_ARG, "null weight or output");
+  if (!is_device_pointer(out)) return fail(ctx, SC_INVALID_ARG, "out must be device (or managed) memory");
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  return check_cuda(ctx, launch_dequantize(w, out, static_cast<cudaStream_t>(stream)), "dequantize launch");
+}
+
+sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* bytes) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (w == nullptr || bytes == nullptr || m < 0) return fail(ctx, SC_INVALID_ARG, "bad argument");
+  *bytes = (m >= 1 && m <= 32) ? gemv_workspace_bytes(w, m, ctx->sm_count) : 0;
+  return SC_OK;
+}
+
+sc_status sc_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  return run_linear(ctx, w, x, m, bias, y, false, workspace, workspace_bytes, stream, 0);
+}
+
+sc_status sc_linear_ex(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, void* y,
+                       sc_out_type y_type, void* workspace, size_t workspace_bytes, void* stream) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (y_type != SC_OUT_BF16 && y_type != SC_OUT_F32) return fail(ctx, SC_INVALID_ARG, "unknown output type");
+  return run_linear(ctx, w, x, m, bias, y, y_type == SC_OUT_F32, workspace, workspace_bytes, stream, 0);
+}
+
+sc_status sc_linear_w8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  return run_linear(ctx, w, x, m, bias, y, false, workspace, workspace_bytes, stream, SC_WEIGHT_INT8);
+}
+
+sc_status sc_linear_fp8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  return run_linear(ctx, w, x, m, bias, y, false, workspace, workspace_bytes, stream, SC_WEIGHT_E4M3);
+}
+
+sc_status sc_gemv_w8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  sc_status s = check_product_args(ctx, w, x, m, bias, y);
+  if (s != SC_OK) return s;
+  if (m > 32) return fail(ctx, SC_UNSUPPORTED_SHAPE, "sc_gemv_w8 takes at most 32 rows");
+  if (m == 0) return SC_OK;
+  if ((s = enter(ctx)) != SC_OK) return s;
+  return run_gemv(ctx, w, x, m, bias, y, false, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+sc_status sc_sync(sc_ctx* ctx, void* stream) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  return check_cuda(ctx, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "cudaStreamSynchronize");
+}
+
+sc_status sc_poll_errors(sc_ctx* ctx, void* stream) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  sc_status s = sc_sync(ctx, stream);
+  if (s != SC_OK) return s;
+  int h[kErrWords] = {0, 0, 0, 0};
+  if ((s = check_cuda(ctx, cudaMemcpy(h, ctx->d_err, sizeof h, cudaMemcpyDeviceToHost), "error word")) != SC_OK) return s;
+  if (h[0] == 0) return SC_OK;
+  cudaMemset(ctx->d_err, 0, sizeof h);
+  char msg[160];
+  std::snprintf(msg, sizeof msg, "a bounded device-side wait gave up (site %d, block %d); the kernel returned early",
+                h[1], h[2]);
+  return fail(ctx, SC_TIMEOUT, msg);
+}
+
+}  // extern "C"

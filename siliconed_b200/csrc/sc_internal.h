@@ -1,0 +1,71 @@
+// Internal definitions shared by the translation units of libsiliconed_cuda.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "siliconed_cuda.h"
+
+// The weight arena's geometry: every weight is stored transposed, [n_pad][k_pad] bytes, K padded
+// to the GEMM's K tile and N to its N tile, so that no TMA box ever leaves the arena.
+namespace sc {
+constexpr int kArenaKAlign = 64;    // the GEMM's BK (one 128-byte swizzle row of bf16)
+constexpr int kArenaNAlign = 256;   // the GEMM's BN
+constexpr int kErrWords = 4;        // device error word: code, site, block, spare
+
+// Codes of the padding: q = 0 in the stored encoding of each kind.
+constexpr uint8_t kPadInt8 = 0x80;  // int8 is stored biased, u = q + 128
+constexpr uint8_t kPadE4M3 = 0x00;  // +0
+}  // namespace sc
+
+typedef CUresult (*sc_encode_tiled_fn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                       const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct sc_ctx {
+  int device = -1;
+  int sm_count = 0;
+  int* d_err = nullptr;  // sc::kErrWords ints on the device
+  sc_encode_tiled_fn encode_tiled = nullptr;
+  std::string last_error;
+};
+
+struct sc_weight {
+  int kind = 0;               // SC_WEIGHT_INT8 / SC_WEIGHT_E4M3
+  int64_t k = 0, n = 0;       // logical shape [K, N]
+  int64_t k_pad = 0, n_pad = 0;
+  uint8_t* arena = nullptr;   // one allocation: values, then fp32 scales at a 256-byte boundary
+  uint8_t* values = nullptr;  // [n_pad][k_pad] stored codes (int8 biased by 128, e4m3 as is)
+  float* scales = nullptr;    // [n_pad] fp32 (0 in the padding)
+  size_t bytes = 0;
+  bool has_nan_codes = false; // e4m3 weight holding NaN codes (0x7F / 0xFF)
+  int device = -1;
+  CUtensorMap tmap_values;    // 2D map over values: inner K (bytes), outer N rows; box 64 x 256
+};
+
+namespace sc {
+
+// Sets ctx->last_error and returns `status`.
+sc_status fail(sc_ctx* ctx, sc_status status, const std::string& message);
+// Maps a CUDA runtime error to SC_CUDA_ERROR with its message (SC_OK if none).
+sc_status check_cuda(sc_ctx* ctx, cudaError_t e, const char* what);
+
+// Kernel launchers (host side), defined beside their kernels.
+cudaError_t launch_retile(const uint8_t* src, bool published_nk, int kind, int64_t k, int64_t n_total, int64_t n_begin,
+                          int64_t n_cols, uint8_t* dst, int64_t k_pad, int64_t n_pad, int* nan_flag,
+                          cudaStream_t stream);
+cudaError_t launch_dequantize(const sc_weight* w, float* out, cudaStream_t stream);
+
+cudaError_t launch_gemm_tc(const CUtensorMap& tmap_x, const sc_weight* w, const uint16_t* bias, void* y, bool f32_out,
+                           int64_t m, int* err, int sm_count, cudaStream_t stream);
+
+// Split count and workspace of the skinny product.
+int gemv_splits(const sc_weight* w, int64_t m, int sm_count);
+size_t gemv_workspace_bytes(const sc_weight* w, int64_t m, int sm_count);
+cudaError_t launch_gemv(const sc_weight* w, const uint16_t* x, int64_t m, const uint16_t* bias, void* y, bool f32_out,
+                        float* workspace, int splits, cudaStream_t stream);
+
+}  // namespace sc

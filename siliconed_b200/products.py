@@ -1,0 +1,226 @@
+"""Host-side mirror of Siliconed's quantized-linear interface, over the C ABI.
+
+``WeightProducts.linear(name, a, c, m, k, n)`` keeps the reference's entry point
+(Sources/Siliconed/WeightProducts.swift:278-279: the product ``C = A . W`` of the map's weight
+``name``), and ``QuantizedWeight`` plays the map tensor + its ``Scale`` (Artifact.swift:15-57).
+PyTorch is used here only to hold device buffers and to name the caller's CUDA stream; every
+product runs in libsiliconed_cuda.  Errors raise ``SiliconedError`` (the reference throws).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import abi
+from .abi import SiliconedError, check
+
+try:  # torch is the device-memory plumbing of this host layer, not part of the library
+    import torch
+except ImportError:  # pragma: no cover
+    torch = None
+
+
+def _stream_ptr(stream) -> ctypes.c_void_p:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    if hasattr(stream, "cuda_stream"):
+        stream = stream.cuda_stream
+    return ctypes.c_void_p(int(stream))
+
+
+def _ptr(t) -> ctypes.c_void_p:
+    if t is None:
+        return ctypes.c_void_p(0)
+    if torch is not None and isinstance(t, torch.Tensor):
+        return ctypes.c_void_p(t.data_ptr())
+    return t.ctypes.data_as(ctypes.c_void_p)
+
+
+class Context:
+    """An sc_ctx on one CUDA device."""
+
+    def __init__(self, device: int = 0):
+        self.lib = abi.load()
+        self.device = int(device)
+        p = ctypes.c_void_p()
+        status = self.lib.sc_ctx_create(self.device, ctypes.byref(p))
+        if status != abi.OK:
+            raise SiliconedError(status, f"sc_ctx_create({device})")
+        self.ptr = p
+
+    def close(self) -> None:
+        if getattr(self, "ptr", None):
+            self.lib.sc_ctx_destroy(self.ptr)
+            self.ptr = None
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, status: int) -> None:
+        check(status, self.ptr)
+
+    def sync(self, stream=None) -> None:
+        self.check(self.lib.sc_sync(self.ptr, _stream_ptr(stream)))
+
+    def poll_errors(self, stream=None) -> None:
+        """Raises SiliconedError(SC_TIMEOUT) if a bounded device-side wait gave up since the last poll."""
+        self.check(self.lib.sc_poll_errors(self.ptr, _stream_ptr(stream)))
+
+
+def _scale_type_of(scales) -> tuple[int, object]:
+    """(sc_scale_type, contiguous host-or-device buffer) of a scale array as published."""
+    if torch is not None and isinstance(scales, torch.Tensor):
+        t = scales.contiguous()
+        kinds = {torch.float32: abi.SCALE_F32, torch.bfloat16: abi.SCALE_BF16, torch.float16: abi.SCALE_F16}
+        if t.dtype not in kinds:
+            raise SiliconedError(abi.INVALID_ARG, f"scale dtype {t.dtype}")
+        return kinds[t.dtype], t
+    a = np.ascontiguousarray(scales)
+    kinds = {np.dtype(np.float32): abi.SCALE_F32, np.dtype(np.float16): abi.SCALE_F16}
+    if a.dtype not in kinds:
+        raise SiliconedError(abi.INVALID_ARG, f"scale dtype {a.dtype} (pass bf16 bits with scale_type=SCALE_BF16)")
+    return kinds[a.dtype], a
+
+
+class QuantizedWeight:
+    """One 8-bit linear weight registered in the library's device arena.
+
+    values: [K, N] codes in the map's layout (or [N, K] with ``published_nk``), int8 / uint8 bytes, as a
+    numpy array or a torch tensor (CPU or CUDA).  scales: one per output (shape [N]) or one for the
+    tensor (shape [] / [1]), fp32 / bf16 / fp16.  ``columns=(n0, n1)`` keeps only that column shard.
+    """
+
+    def __init__(self, ctx: Context, values, kind: int, scales, *, scale_type: int | None = None,
+                 published_nk: bool = False, columns: tuple[int, int] | None = None, stream=None):
+        self.ctx = ctx
+        lib = ctx.lib
+        on_device = torch is not None and isinstance(values, torch.Tensor) and values.is_cuda
+        if torch is not None and isinstance(values, torch.Tensor):
+            v = values.contiguous()
+            if v.dtype not in (torch.int8, torch.uint8):
+                v = v.view(torch.uint8) if v.element_size() == 1 else None
+            if v is None:
+                raise SiliconedError(abi.INVALID_ARG, "values must be 1-byte codes")
+            shape = tuple(v.shape)
+        else:
+            v = np.ascontiguousarray(values)
+            if v.dtype.itemsize != 1:
+                raise SiliconedError(abi.INVALID_ARG, "values must be 1-byte codes")
+            shape = v.shape
+        if len(shape) != 2:
+            raise SiliconedError(abi.INVALID_ARG, "values must be 2-D")
+        k, n = (shape[1], shape[0]) if published_nk else shape
+        st, s = _scale_type_of(scales)
+        if scale_type is not None:
+            st = scale_type
+        s_count = int(np.prod(s.shape)) if len(s.shape) else 1
+        layout = abi.SCALE_TENSOR if s_count == 1 else abi.SCALE_COLUMNS
+        if layout == abi.SCALE_COLUMNS and s_count != n:
+            raise SiliconedError(abi.INVALID_ARG, f"{s_count} scales for {n} outputs")
+        s_on_device = torch is not None and isinstance(s, torch.Tensor) and s.is_cuda
+        if on_device != s_on_device:
+            s = s.to(values.device) if on_device else (s.cpu() if isinstance(s, torch.Tensor) else s)
+        flags = (abi.VALUES_ON_DEVICE if on_device else 0) | (abi.PUBLISHED_NK if published_nk else 0)
+        n0, n1 = columns if columns is not None else (0, n)
+        p = ctypes.c_void_p()
+        self._keep = (v, s)
+        ctx.check(lib.sc_weight_create_shard(ctx.ptr, _ptr(v), kind, k, n, _ptr(s), st, layout, flags, n0, n1,
+                                             _stream_ptr(stream) if torch is not None else None, ctypes.byref(p)))
+        self._keep = None
+        self.ptr = p
+        self.kind = kind
+        self.k, self.n = int(k), int(n1 - n0)
+        bk, bn, kd, by = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int(), ctypes.c_size_t()
+        ctx.check(lib.sc_weight_info(self.ptr, ctypes.byref(bk), ctypes.byref(bn), ctypes.byref(kd),
+                                     ctypes.byref(by)))
+        self.device_bytes = int(by.value)
+
+    def close(self) -> None:
+        if getattr(self, "ptr", None):
+            self.ctx.lib.sc_weight_destroy(self.ctx.ptr, self.ptr)
+            self.ptr = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def workspace_bytes(self, m: int) -> int:
+        b = ctypes.c_size_t()
+        self.ctx.check(self.ctx.lib.sc_workspace_size(self.ctx.ptr, self.ptr, int(m), ctypes.byref(b)))
+        return int(b.value)
+
+    def dequantize(self, out=None, stream=None):
+        """fp32 [K, N] on the device: float(q) * s, bit for bit (Widen.dequantize)."""
+        if out is None:
+            out = torch.empty((self.k, self.n), dtype=torch.float32, device=f"cuda:{self.ctx.device}")
+        self.ctx.check(self.ctx.lib.sc_dequantize(self.ctx.ptr, self.ptr, _ptr(out), _stream_ptr(stream)))
+        return out
+
+    def _product(self, fn_name: str, x, bias, out, workspace, stream):
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.shape[1] != self.k:
+            raise SiliconedError(abi.INVALID_ARG, f"x must be a CUDA bf16 [M, {self.k}] tensor")
+        x = x.contiguous()
+        m = x.shape[0]
+        if out is None:
+            out = torch.empty((m, self.n), dtype=torch.bfloat16, device=x.device)
+        need = self.workspace_bytes(m)
+        if need and workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+        ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        fn = getattr(self.ctx.lib, fn_name)
+        self.ctx.check(fn(self.ctx.ptr, self.ptr, _ptr(x), m, _ptr(bias), _ptr(out), _ptr(workspace), ws_bytes,
+                          _stream_ptr(stream)))
+        return out
+
+    def linear(self, x, bias=None, out=None, workspace=None, stream=None):
+        """y = bf16((x . q) * s + bias), dispatching on M (GEMV for M <= 32, tensor-core GEMM above)."""
+        return self._product("sc_linear", x, bias, out, workspace, stream)
+
+    def gemv(self, x, bias=None, out=None, workspace=None, stream=None):
+        return self._product("sc_gemv_w8", x, bias, out, workspace, stream)
+
+
+class WeightProducts:
+    """Products by weight name: the reference's ``WeightProducts.linear(_:a:c:m:k:n:)``.
+
+    ``register`` stands for the map's tensor + scale (the reference reads them from the mmap'd
+    map); ``linear`` computes ``c[m, n] = a[m, k] . W(name)`` into the caller's buffer ``c``.
+    """
+
+    def __init__(self, ctx: Context):
+        self.ctx = ctx
+        self.weights: dict[str, QuantizedWeight] = {}
+        self.biases: dict[str, object] = {}
+        self._workspace = None
+
+    def register(self, name: str, values, kind: int, scales, bias=None, **kw) -> QuantizedWeight:
+        w = QuantizedWeight(self.ctx, values, kind, scales, **kw)
+        self.weights[name] = w
+        if bias is not None:
+            self.biases[name] = bias
+        return w
+
+    def linear(self, name: str, a, c, m: int, k: int, n: int, stream=None) -> None:
+        w = self.weights.get(name)
+        if w is None:
+            raise SiliconedError(abi.INVALID_ARG, f"{name}: no such weight")
+        if (w.k, w.n) != (k, n) or tuple(a.shape) != (m, k) or tuple(c.shape) != (m, n):
+            raise SiliconedError(abi.UNSUPPORTED_SHAPE, f"{name}: [{m}, {k}] . [{w.k}, {w.n}] -> {tuple(c.shape)}")
+        need = w.workspace_bytes(m)
+        ws = None
+        if need:
+            if self._workspace is None or self._workspace.numel() < need:
+                self._workspace = torch.empty(need, dtype=torch.uint8, device=a.device)
+            ws = self._workspace
+        w.linear(a, bias=self.biases.get(name), out=c, workspace=ws, stream=stream)
+
+    def close(self) -> None:
+        for w in self.weights.values():
+            w.close()
+        self.weights.clear()
