@@ -116,8 +116,10 @@ sc_status make_tmap_w(sc_ctx* ctx, sc_weight* w) {
 sc_status check_product_args(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
                              const void* y) {
   if (ctx == nullptr) return SC_INVALID_ARG;
-  if (w == nullptr || x == nullptr || y == nullptr) return fail(ctx, SC_INVALID_ARG, "null weight, x or y");
+  if (w == nullptr) return fail(ctx, SC_INVALID_ARG, "null weight");
   if (m < 0) return fail(ctx, SC_INVALID_ARG, "m < 0");
+  if (m == 0) return SC_OK;  // nothing is read or written: x and y may be null
+  if (x == nullptr || y == nullptr) return fail(ctx, SC_INVALID_ARG, "null x or y");
   if (m > 0x7FFFFFFF || w->k > 0x7FFFFFFF) return fail(ctx, SC_UNSUPPORTED_SHAPE, "m or k beyond 2^31 - 1");
   if (w->device != ctx->device) return fail(ctx, SC_INVALID_ARG, "weight registered on another device");
   if (w->k % 8 != 0) return fail(ctx, SC_UNSUPPORTED_SHAPE, "K must be a multiple of 8 (16-byte activation rows)");
