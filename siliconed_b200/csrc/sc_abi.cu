@@ -104,12 +104,17 @@ sc_status make_tmap_x(sc_ctx* ctx, const sc_bf16* x, int64_t m, int64_t k, CUten
 sc_status make_tmap_w(sc_ctx* ctx, sc_weight* w) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w->k_pad), static_cast<cuuint64_t>(w->n_pad)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w->k_pad)};
-  const cuuint32_t box[2] = {64, 256};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = ctx->encode_tiled(&w->tmap_values, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->values, dims, strides, box, estr,
-                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(ctx, SC_CUDA_ERROR, "cuTensorMapEncodeTiled (weights) failed: " + std::to_string(r));
+  CUtensorMap* maps[2] = {&w->tmap_values, &w->tmap_values_half};
+  const cuuint32_t rows[2] = {256, 128};
+  for (int i = 0; i < 2; ++i) {
+    const cuuint32_t box[2] = {64, rows[i]};
+    CUresult r = ctx->encode_tiled(maps[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->values, dims, strides, box, estr,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(ctx, SC_CUDA_ERROR, "cuTensorMapEncodeTiled (weights) failed: " + std::to_string(r));
+  }
   return SC_OK;
 }
 
@@ -155,6 +160,9 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
   if (m <= 32) return run_gemv(ctx, w, x, m, bias, y, f32_out, workspace, workspace_bytes, st);
   CUtensorMap tmx;
   if ((s = make_tmap_x(ctx, x, m, w->k, &tmx)) != SC_OK) return s;
+  if (m > kPairMinRows)
+    return check_cuda(ctx, launch_gemm_pair(tmx, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
+                      "pair gemm launch");
   return check_cuda(ctx, launch_gemm_tc(tmx, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st), "gemm launch");
 }
 

@@ -285,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -44,6 +44,7 @@ struct sc_weight {
   bool has_nan_codes = false; // e4m3 weight holding NaN codes (0x7F / 0xFF)
   int device = -1;
   CUtensorMap tmap_values;    // 2D map over values: inner K (bytes), outer N rows; box 64 x 256
+  CUtensorMap tmap_values_half;  // the same, box 64 x 128 (the half tile one CTA of a pair converts)
 };
 
 namespace sc {
@@ -61,6 +62,10 @@ cudaError_t launch_dequantize(const sc_weight* w, float* out, cudaStream_t strea
 
 cudaError_t launch_gemm_tc(const CUtensorMap& tmap_x, const sc_weight* w, const uint16_t* bias, void* y, bool f32_out,
                            int64_t m, int* err, int sm_count, cudaStream_t stream);
+cudaError_t launch_gemm_pair(const CUtensorMap& tmap_x, const sc_weight* w, const uint16_t* bias, void* y,
+                             bool f32_out, int64_t m, int* err, int sm_count, cudaStream_t stream);
+// Rows above which the CTA-pair GEMM takes over from the single-CTA one.
+constexpr int64_t kPairMinRows = 128;
 
 // Split count and workspace of the skinny product.
 int gemv_splits(const sc_weight* w, int64_t m, int sm_count);
