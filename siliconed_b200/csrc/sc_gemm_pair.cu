@@ -10,15 +10,28 @@
 // bounds this product on B200.
 //
 // Warp roles in each CTA: warp 0 TMA producer; warp 1 TMEM allocation and (leader only) the MMA
-// issuer; warps 4..7 epilogue (TMEM lane quarters 0..3); warps 8..15 converters.  Cross-CTA
-// signalling: converters arrive on the leader's b_full (release at cluster scope); the leader
-// commits MMA completion to the barriers of both CTAs (one commit per CTA); both epilogues arrive
-// on the leader's acc_empty.  No load of this kernel uses cluster multicast.  Every wait is bounded.
+// issuer; warps 4..7 epilogue (TMEM lane quarters 0..3); warps 8..23 converters.  Cross-CTA
+// signalling: converters arrive on the leader's b_full; the leader's commits of MMA completion
+// arrive on the barriers of both CTAs at once; both epilogues arrive on the leader's acc_empty.  No
+// load of this kernel uses cluster multicast (only the completion signal is sent to both CTAs).
+// Every wait is bounded.
 #include <cuda_bf16.h>
 
 #include "sc_codes.cuh"
 #include "sc_internal.h"
 #include "sc_ptx.cuh"
+
+// Pipeline timestamps of the first CTA pair, compiled only into diagnostic builds (-DSC_TRACE).
+#ifdef SC_TRACE
+__device__ unsigned long long g_sc_trace[2][16][512];
+#define SC_TRACE_EV(ev, idx) \
+  if (blockIdx.x < 2 && (idx) < 512) g_sc_trace[blockIdx.x][(ev)][(idx)] = clock64()
+extern "C" __attribute__((visibility("default"))) int sc_debug_trace(void* host, size_t bytes) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, g_sc_trace, bytes < sizeof(g_sc_trace) ? bytes : sizeof(g_sc_trace)));
+}
+#else
+#define SC_TRACE_EV(ev, idx)
+#endif
 
 namespace sc {
 namespace gemm_pair {
@@ -27,35 +40,40 @@ constexpr int BM = 128;            // rows of x per CTA (256 per pair)
 constexpr int BN = 256;            // output columns per pair tile (the accumulator's width)
 constexpr int BNH = BN / 2;        // weight columns each CTA holds and converts
 constexpr int BK = 64;
-constexpr int kStagesIn = 5;       // x + code tiles in flight
-constexpr int kStagesB = 4;        // converted bf16 weight tiles
+constexpr int kStages = 5;         // ring of stages: x tile, code half-tile and its bf16 conversion
 constexpr int kABytes = BM * BK * 2;
 constexpr int kWBytes = BNH * BK;
 constexpr int kBBytes = BNH * BK * 2;
-constexpr int kWarps = 16;
+constexpr int kWarps = 24;
 constexpr int kThreads = kWarps * 32;
 constexpr int kEpiWarp0 = 4, kEpiWarps = 4;
-constexpr int kConvWarp0 = 8, kConvWarps = 8;
-constexpr int kConvThreads = kConvWarps * 32;
+constexpr int kConvWarp0 = 8, kConvWarps = 16;  // warps 8..23
+constexpr int kConvGroups = 2;                  // groups convert alternate stages concurrently
+constexpr int kGroupThreads = kConvWarps * 32 / kConvGroups;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kChunks = BNH * BK / 8;  // 8-code chunks (one 16-byte bf16 chunk each) per stage
 
-static_assert(kChunks % kConvThreads == 0, "converter work must divide evenly");
+static_assert(kChunks % kGroupThreads == 0, "converter work must divide evenly");
+
+// Converter thread index of warp `warp`, or -1.
+__device__ __forceinline__ int converter_index(int warp, int lane) {
+  return warp >= kConvWarp0 ? (warp - kConvWarp0) * 32 + lane : -1;
+}
 
 struct __align__(1024) Smem {
-  uint8_t a[kStagesIn][kABytes];  // x tiles, 128-byte swizzled (TMA)
-  uint8_t b[kStagesB][kBBytes];   // converted weight half-tiles, 128-byte swizzled
-  uint8_t w[kStagesIn][kWBytes];  // code half-tiles (TMA)
+  uint8_t a[kStages][kABytes];    // x tiles, 128-byte swizzled (TMA)
+  uint8_t b[kStages][kBBytes];    // converted weight half-tiles, 128-byte swizzled
+  uint8_t w[kStages][kWBytes];    // code half-tiles (TMA)
   float sb[kEpiWarps][2][BN];     // per epilogue warp: the tile's scales and biases
-  uint64_t in_full[kStagesIn];
-  uint64_t in_empty[kStagesIn];
-  uint64_t b_full[kStagesB];      // leader: both CTAs' converters
-  uint64_t b_empty[kStagesB];
+  uint64_t full[kStages];         // this CTA's x and code tiles landed
+  uint64_t b_full[kStages];       // leader: both CTAs converted the stage
+  uint64_t empty[kStages];        // the pair's MMAs of the stage completed (leader's commit)
   uint64_t acc_full[2];
   uint64_t acc_empty[2];          // leader: both CTAs' epilogues
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  int conv_ok[kConvGroups];       // each converter group's elected thread's wait outcome
 };
 
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
@@ -93,13 +111,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = &s.abort;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStagesIn; ++i) {
-      mbar_init(&s.in_full[i], 1);
-      mbar_init(&s.in_empty[i], 1 + kConvWarps);  // the leader's commit + this CTA's converter warps
-    }
-    for (int i = 0; i < kStagesB; ++i) {
-      mbar_init(&s.b_full[i], 2 * kConvWarps);
-      mbar_init(&s.b_empty[i], 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.b_full[i], 2);    // one elected converter thread per CTA
+      mbar_init(&s.empty[i], 1);     // the leader's commit
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full[i], 1);
@@ -124,67 +139,73 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer (each CTA loads its own halves) ----------------
     if (lane == 0) {
-      int stage = 0;
+      int stage = 0, gcount = 0;
       uint32_t phase = 0, issued = 0, last_parity = 0;
       for (int tile = pair; tile < num_tiles && !*abort; tile += pairs) {
         const int mt = tile % m_tiles, nt = tile / m_tiles;
         const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM;
         const int col0 = nt * BN + static_cast<int>(rank) * BNH;
         for (int kt = 0; kt < k_tiles; ++kt) {
-          if (!mbar_wait_cluster(&s.in_empty[stage], phase ^ 1u, abort, err, kSiteProducerEmpty)) break;
-          mbar_arrive_expect_tx(&s.in_full[stage], kABytes + kWBytes);
-          tma_load_2d(s.a[stage], &tm_x, &s.in_full[stage], kt * BK, row0);
-          tma_load_2d(s.w[stage], &tm_w, &s.in_full[stage], kt * BK, col0);
+          if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort, err, kSiteProducerEmpty)) break;
+          mbar_arrive_expect_tx(&s.full[stage], kABytes + kWBytes);
+          SC_TRACE_EV(0, gcount);
+          tma_load_2d(s.a[stage], &tm_x, &s.full[stage], kt * BK, row0);
+          tma_load_2d(s.w[stage], &tm_w, &s.full[stage], kt * BK, col0);
           issued |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == kStagesIn) {
+          ++gcount;
+          if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      for (int st = 0; st < kStagesIn; ++st)
-        if (issued & (1u << st)) mbar_wait_drain(&s.in_full[st], (last_parity >> st) & 1u);
+      for (int st = 0; st < kStages; ++st)
+        if (issued & (1u << st)) mbar_wait_drain(&s.full[st], (last_parity >> st) & 1u);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA) ----------------
     if (leader && lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(2 * BM, BN);
-      int stage = 0, bstage = 0, acc = 0;
-      uint32_t phase = 0, bphase = 0, acc_phase = 0;
+      int stage = 0, acc = 0, gcount = 0;
+      uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += pairs) {
-        if (!mbar_wait_cluster(&s.acc_empty[acc], acc_phase ^ 1u, abort, err, kSiteMmaAccum)) break;
+        if (!mbar_wait(&s.acc_empty[acc], acc_phase ^ 1u, abort, err, kSiteMmaAccum)) break;
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(acc * BN);
+        // The next stage's barrier is probed before the current stage's MMAs are issued, and the
+        // blocking wait runs only when that probe found it incomplete: no barrier operation sits
+        // between the last MMA of one stage and the first of the next.
+        bool ready = mbar_test_wait(&s.b_full[stage], phase);
         for (int kt = 0; kt < k_tiles; ++kt) {
           // Both CTAs' converters arrive here only after their own x and code tiles landed.
-          if (!mbar_wait_cluster(&s.b_full[bstage], bphase, abort, err, kSiteMmaConverted)) {
+          if (!ready && !mbar_poll(&s.b_full[stage], phase, abort, err, kSiteMmaConverted)) {
             ok = false;
             break;
           }
+          SC_TRACE_EV(4, gcount);
           tc_fence_after();
-          const uint32_t a0 = smem_u32(s.a[stage]), b0 = smem_u32(s.b[bstage]);
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            tc_mma_f16_pair(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
-                            (kt | kk) != 0 ? 1u : 0u);
-          tc_commit_pair(peer_addr(&s.in_empty[stage], 0));
-          tc_commit_pair(peer_addr(&s.in_empty[stage], 1));
-          tc_commit_pair(peer_addr(&s.b_empty[bstage], 0));
-          tc_commit_pair(peer_addr(&s.b_empty[bstage], 1));
-          if (++stage == kStagesIn) {
+          const int cur = stage;
+          if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
-          if (++bstage == kStagesB) {
-            bstage = 0;
-            bphase ^= 1u;
+          ready = kt + 1 < k_tiles && mbar_test_wait(&s.b_full[stage], phase);
+          SC_TRACE_EV(11, gcount);
+          const uint32_t a0 = smem_u32(s.a[cur]), b0 = smem_u32(s.b[cur]);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            tc_mma_f16_pair(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
+                            (kt | kk) != 0 ? 1u : 0u);
+            SC_TRACE_EV(12 + kk, gcount);
           }
+          tc_commit_pair_both(&s.empty[cur], 0x3);
+          SC_TRACE_EV(5, gcount);
+          ++gcount;
         }
         if (!ok) break;
-        tc_commit_pair(peer_addr(&s.acc_full[acc], 0));
-        tc_commit_pair(peer_addr(&s.acc_full[acc], 1));
+        tc_commit_pair_both(&s.acc_full[acc], 0x3);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
@@ -210,7 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         s_bias[c] = (bias != nullptr && n < N) ? __uint_as_float(static_cast<uint32_t>(bias[n]) << 16) : 0.0f;
       }
       __syncwarp();
-      if (!mbar_wait_cluster(&s.acc_full[acc], acc_phase, abort, err, kSiteEpilogueFull)) break;
+      int ready = 0;
+      if (lane == 0) ready = mbar_wait(&s.acc_full[acc], acc_phase, abort, err, kSiteEpilogueFull) ? 1 : 0;
+      if (!__shfl_sync(0xFFFFFFFFu, ready, 0)) break;
+      if (threadIdx.x == kEpiWarp0 * 32) SC_TRACE_EV(6, (tile - pair) / pairs);
       tc_fence_after();
       const uint32_t tbase = tmem + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
@@ -265,48 +289,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(peer_addr(&s.acc_empty[acc], 0));
+      if (threadIdx.x == kEpiWarp0 * 32) SC_TRACE_EV(7, (tile - pair) / pairs);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-  } else if (warp >= kConvWarp0) {
+  } else if (converter_index(warp, lane) >= 0) {
     // ---------------- converters (each CTA: its 128 weight columns) ----------------
-    const int ct = threadIdx.x - kConvWarp0 * 32;
-    int stage = 0, bstage = 0;
-    uint32_t phase = 0, bphase = 0;
-    bool ok = true;
-    for (int tile = pair; tile < num_tiles && ok; tile += pairs) {
-      for (int kt = 0; kt < k_tiles; ++kt) {
-        if (!mbar_wait(&s.in_full[stage], phase, abort, err, kSiteConverterFull) ||
-            !mbar_wait_cluster(&s.b_empty[bstage], bphase ^ 1u, abort, err, kSiteConverterSlot)) {
-          ok = false;
-          break;
-        }
-        const uint8_t* src = s.w[stage];
-        uint8_t* dst = s.b[bstage];
+    // kConvGroups groups take the K stages in turn (group g: stages g, g + G, ...), so several
+    // stages are converted at once.  In a group, one elected thread waits for the stage; a named
+    // barrier hands its outcome to the group (all its threads take the same path and always meet at
+    // the next barrier); after the conversion a second named barrier gathers the group and the
+    // elected thread signals the leader's MMA and this CTA's producer.
+    const int cidx = converter_index(warp, lane);
+    const int group = cidx / kGroupThreads, ct = cidx % kGroupThreads;
+    const int bar_id = 1 + group;
+    const int total = ((num_tiles - pair + pairs - 1) / pairs) * k_tiles;  // K stages this CTA runs
+    for (int g = group; g < total; g += kConvGroups) {
+      // The producer refilled this stage only after the pair's MMAs of its previous round completed,
+      // so the bf16 slot of the stage is free as soon as the new code tile has landed.
+      const int stage = g % kStages;
+      const uint32_t phase = static_cast<uint32_t>(g / kStages) & 1u;
+      if (ct == 0) {
+        const bool got = mbar_wait(&s.full[stage], phase, abort, err, kSiteConverterFull);
+        SC_TRACE_EV(1, g);
+        SC_TRACE_EV(2, g);
+        s.conv_ok[group] = got;
+      }
+      named_barrier_sync(bar_id, kGroupThreads);
+      if (ct == 0) SC_TRACE_EV(8, g);
+      if (!s.conv_ok[group]) break;
+      const uint8_t* src = s.w[stage];
+      uint8_t* dst = s.b[stage];
+      // Eight consecutive threads write the eight 16-byte chunks of one 128-byte row; all loads of a
+      // thread are issued before its conversions.
+      constexpr int kPer = kChunks / kGroupThreads;
+      uint2 in[kPer];
 #pragma unroll
-        for (int i = 0; i < kChunks / kConvThreads; ++i) {
-          // Eight consecutive threads write the eight 16-byte chunks of one 128-byte row: no bank
-          // conflict whatever the swizzle.
-          const int c = ct + i * kConvThreads;
-          const int row = c >> 3, j = c & 7;
-          const uint2 in = *reinterpret_cast<const uint2*>(src + row * BK + j * 8);
-          *reinterpret_cast<uint4*>(dst + row * (BK * 2) + ((j ^ (row & 7)) << 4)) =
-              codes8_to_bf16<kKind, kNaN>(in.x, in.y);
-        }
-        fence_async_all();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_cluster(peer_addr(&s.b_full[bstage], 0));
-          mbar_arrive(&s.in_empty[stage]);
-        }
-        if (++stage == kStagesIn) {
-          stage = 0;
-          phase ^= 1u;
-        }
-        if (++bstage == kStagesB) {
-          bstage = 0;
-          bphase ^= 1u;
-        }
+      for (int i = 0; i < kPer; ++i) {
+        const int c = ct + i * kGroupThreads;
+        in[i] = *reinterpret_cast<const uint2*>(src + (c >> 3) * BK + (c & 7) * 8);
+      }
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int c = ct + i * kGroupThreads;
+        const int row = c >> 3, j = c & 7;
+        *reinterpret_cast<uint4*>(dst + row * (BK * 2) + ((j ^ (row & 7)) << 4)) =
+            codes8_to_bf16<kKind, kNaN>(in[i].x, in[i].y);
+      }
+      if (ct == 0) SC_TRACE_EV(9, g);
+      fence_async_shared();
+      if (ct == 0) SC_TRACE_EV(10, g);
+      named_barrier_sync(bar_id, kGroupThreads);
+      if (ct == 0) {
+        SC_TRACE_EV(3, g);
+        if (leader) mbar_arrive(&s.b_full[stage]);
+        else mbar_arrive_cluster(peer_addr(&s.b_full[stage], 0));
       }
     }
   }

@@ -66,6 +66,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-suspending probe of a phase (the thread keeps its issue slot; for latency-critical pollers).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Records the first error of a launch: code, site, block.
 __device__ __forceinline__ void record_error(int* err, int code, int site) {
   if (err != nullptr && atomicCAS(err, 0, code) == 0) {
@@ -82,6 +95,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 31u) == 0u) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        record_error(err, kErrTimeout, site);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// mbar_wait by polling with the non-suspending probe.
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 255u) == 0u) {
       if (*abort) return false;
       if (global_ns() - t0 > kWaitLimitNs) {
         record_error(err, kErrTimeout, site);
@@ -172,6 +202,11 @@ __device__ __forceinline__ void tmem_ld_32(uint32_t taddr, uint32_t (&r)[32]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Named barrier `id` (1..15) over `threads` threads (a multiple of 32); every thread named must arrive.
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ---- clusters and CTA pairs ---------------------------------------------------------------
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -187,9 +222,11 @@ __device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t rank) 
   return r;
 }
 
-// Arrive (release at cluster scope) on an mbarrier given by its shared::cluster address.
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's).  Default
+// (CTA-scope release) semantics: the data it announces is in the arriving CTA's own shared memory,
+// made visible to the tensor cores beforehand by the async-proxy fence.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
@@ -259,6 +296,16 @@ __device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t adesc,
 __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
                : "memory");
+}
+
+// Arrives once on the mbarrier at the same shared-memory offset in each CTA of `cta_mask` when the
+// pair MMAs this thread issued have completed (a commit, not a load: no data moves).
+__device__ __forceinline__ void tc_commit_pair_both(const uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
 }
 
 // Shared-memory matrix descriptor of a K-major, 128-byte-swizzled bf16 tile: rows of 64 elements
