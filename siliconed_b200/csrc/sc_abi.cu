@@ -144,7 +144,7 @@ sc_status run_gemv(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m,
   if (workspace_bytes < need || (need > 0 && workspace == nullptr))
     return fail(ctx, SC_WORKSPACE_TOO_SMALL, "workspace smaller than sc_workspace_size");
   const int splits = gemv_splits(w, m, ctx->sm_count);
-  return check_cuda(ctx, launch_gemv(w, x, m, bias, y, f32_out, static_cast<float*>(workspace), splits, st),
+  return check_cuda(ctx, launch_gemv(w, x, m, bias, y, f32_out, static_cast<float*>(workspace), splits, ctx->d_err, st),
                     "gemv launch");
 }
 

@@ -67,10 +67,10 @@ cudaError_t launch_gemm_pair(const CUtensorMap& tmap_x, const sc_weight* w, cons
 // Rows above which the CTA-pair GEMM takes over from the single-CTA one.
 constexpr int64_t kPairMinRows = 128;
 
-// Split count and workspace of the skinny product.
+// CTA count and workspace of the skinny product.
 int gemv_splits(const sc_weight* w, int64_t m, int sm_count);
 size_t gemv_workspace_bytes(const sc_weight* w, int64_t m, int sm_count);
 cudaError_t launch_gemv(const sc_weight* w, const uint16_t* x, int64_t m, const uint16_t* bias, void* y, bool f32_out,
-                        float* workspace, int splits, cudaStream_t stream);
+                        float* workspace, int splits, int* err, cudaStream_t stream);
 
 }  // namespace sc
