@@ -125,6 +125,20 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def route_kernels(case, ws_bytes: int) -> list[str]:
+    """The library's kernels one product of this case launches (the step the roofline's `achieved`
+    covers): the GEMV for m <= 32 (one launch per pass of up to 8 rows), the single-CTA GEMM up to
+    128 rows, the fused pair kernel above, and from 1536 rows with a workspace the widening of the
+    codes followed by the bf16-operand pair GEMM."""
+    if case.m <= 32:
+        return ["gemv_w8"] * (-(-case.m // 8))
+    if case.m <= 128:
+        return ["gemm_w8_tc"]
+    if ws_bytes > 0:
+        return ["widen_codes", "gemm_bf16_pair"]
+    return ["gemm_w8_pair"]
+
+
 def cpu_baseline(case, budget_s: float = 12.0):
     """The reference's CPU path restated (the oracle): dequantize W (OpenMP, all host threads), then
     an fp32 GEMM on the CPU (torch.matmul, all threads), on a bounded sample of the rows."""
@@ -284,13 +298,14 @@ def run_ours(args):
                 "config": dict(describe(case, args.workload), parallelism=f"replicas x{world} (batch-sharded)"),
                 "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": runit,
                              "frac": achieved / peak, "traffic": traffic,
-                             "peak_source": f"{peak_src} (burst figure: the kernel is timed alone)"},
+                             "peak_source": f"{peak_src} (burst figure: the kernel is timed alone)",
+                             "kernels": route_kernels(case, ws_bytes)},
                 "clocks": clocks.summary(),
                 "e2e": {"value": e2e_value, "unit": unit,
                         "h2d_bytes_per_step": int(case.x.nbytes),
                         "d2h_bytes_per_step": int(case.m * case.n * 2),
                         "path": "QuantizedWeight.linear (sc_linear) with pinned host x / y copied in the timed region"},
-                "gpu_launches": args.steps * (1 if case.m > 32 else -(-case.m // 8)),
+                "gpu_launches": args.steps * len(route_kernels(case, ws_bytes)),
                 "step_ms_min": min(per_step), "step_ms_median": statistics.median(per_step)}
         if not args.no_cpu_baseline:
             per, flops, byts, threads, rows, reps = cpu_baseline(case)

@@ -123,7 +123,13 @@ SC_API sc_status sc_dequantize(sc_ctx* ctx, const sc_weight* w, float* out, void
 /* ---- products ----------------------------------------------------------------------------- */
 
 /* Scratch bytes a product of `m` rows on `w` needs (0 when it needs none).  The caller owns the
- * workspace; the library allocates nothing on the product path (WeightProducts.swift:50-53). */
+ * workspace; the library allocates nothing on the product path (WeightProducts.swift:50-53).
+ * From m = 1536 rows it is n_pad * k_pad * 2 bytes (N rounded up to 256, K to 64): the weight's
+ * codes widened once to bf16, then a GEMM on bf16 operands, which beats converting the codes in
+ * every 256-row block of x.  It must be 256-byte aligned; its contents need no initialisation and
+ * are overwritten by every call, so products that may run at the same time on the GPU need
+ * workspaces of their own.  With a NULL or smaller workspace such a product runs the fused kernel
+ * instead; both routes give the same bits. */
 SC_API sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* bytes);
 
 /*
@@ -135,7 +141,7 @@ SC_API sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, s
  * widened route (WeightProducts.swift:995-1001 -> GEMM.linear, GEMM.swift:297-345).
  * Dispatches on the weight's kind and on m: m <= 32 runs the skinny GEMV, larger m the
  * tensor-core GEMM.  x, y, bias: device pointers, 16-byte aligned; K a multiple of 8.
- * workspace may be NULL when sc_workspace_size reports 0.
+ * workspace may be NULL when sc_workspace_size reports 0 (and from 1536 rows, at the cost of speed).
  */
 SC_API sc_status sc_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
                     void* workspace, size_t workspace_bytes, void* stream);

@@ -101,6 +101,19 @@ sc_status make_tmap_x(sc_ctx* ctx, const sc_bf16* x, int64_t m, int64_t k, CUten
   return SC_OK;
 }
 
+// Map over the widened bf16 copy [n_pad][k_pad] of a weight: box 64 x 128, 128-byte swizzle.
+sc_status make_tmap_widened(sc_ctx* ctx, const sc_weight* w, void* widened, CUtensorMap* map) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w->k_pad), static_cast<cuuint64_t>(w->n_pad)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w->k_pad) * 2};
+  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, widened, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, SC_CUDA_ERROR, "cuTensorMapEncodeTiled (widened weight) failed: " + std::to_string(r));
+  return SC_OK;
+}
+
 sc_status make_tmap_w(sc_ctx* ctx, sc_weight* w) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w->k_pad), static_cast<cuuint64_t>(w->n_pad)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w->k_pad)};
@@ -160,9 +173,21 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
   if (m <= 32) return run_gemv(ctx, w, x, m, bias, y, f32_out, workspace, workspace_bytes, st);
   CUtensorMap tmx;
   if ((s = make_tmap_x(ctx, x, m, w->k, &tmx)) != SC_OK) return s;
-  if (m > kPairMinRows)
+  if (m > kPairMinRows) {
+    // With a workspace for the widened weight: widen once, then the bf16-operand pair GEMM (the
+    // same operands and summation order as the fused kernel, so the same bits).  Without one: the
+    // fused pair kernel, which converts the codes in shared memory.
+    if (m >= kWidenMinRows && workspace != nullptr && workspace_bytes >= widened_bytes(w) &&
+        (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0) {
+      CUtensorMap tmw;
+      if ((s = make_tmap_widened(ctx, w, workspace, &tmw)) != SC_OK) return s;
+      if ((s = check_cuda(ctx, launch_widen(w, workspace, ctx->sm_count, st), "widen launch")) != SC_OK) return s;
+      return check_cuda(ctx, launch_gemm_bf16(tmx, tmw, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
+                        "bf16 pair gemm launch");
+    }
     return check_cuda(ctx, launch_gemm_pair(tmx, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
                       "pair gemm launch");
+  }
   return check_cuda(ctx, launch_gemm_tc(tmx, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st), "gemm launch");
 }
 
@@ -387,7 +412,9 @@ sc_status sc_dequantize(sc_ctx* ctx, const sc_weight* w, float* out, void* strea
 sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* bytes) {
   if (ctx == nullptr) return SC_INVALID_ARG;
   if (w == nullptr || bytes == nullptr || m < 0) return fail(ctx, SC_INVALID_ARG, "bad argument");
-  *bytes = (m >= 1 && m <= 32) ? gemv_workspace_bytes(w, m, ctx->sm_count) : 0;
+  if (m >= 1 && m <= 32) *bytes = gemv_workspace_bytes(w, m, ctx->sm_count);
+  else if (m >= kWidenMinRows) *bytes = widened_bytes(w);
+  else *bytes = 0;
   return SC_OK;
 }
 

@@ -1,0 +1,342 @@
+// The large-M product in two launches: the weight's codes widened once to bf16 in the caller's
+// workspace, then a CTA-pair tcgen05 GEMM whose two operands both arrive by TMA.
+//
+// In the fused pair kernel (sc_gemm_pair.cu) every CTA pair converts the codes of its weight
+// columns for every K stage of every output tile: each code is converted once per 256-row block of
+// x, and the conversion sits in the pipeline between the code tile's arrival and the MMA.  For
+// large M that costs more than it saves: widening the whole weight once reads K*N bytes and writes
+// 2*K*N (a few microseconds of HBM time), after which the GEMM streams both operands with TMA and
+// nothing but the tensor cores works between a stage's arrival and its MMA.  The widened values are
+// exact (every int8 and e4m3 value is a bf16), the scale and bias are applied in the epilogue after
+// the fp32 sum as in the fused kernel, and the MMAs see the same operands in the same order, so the
+// two routes give the same bits.
+//
+// GEMM layout: a cluster of two CTAs owns output tiles of 256 x 256.  Each CTA loads its own 128
+// rows of x and 128 of the 256 weight columns (bf16, 128-byte swizzled) into a 6-stage ring; the
+// loads use the pair form of the tensor-map copy, so both CTAs' bytes are counted on the leader's
+// barrier, and the leader issues tcgen05.mma.cta_group::2 (M = 256, N = 256) into the fp32
+// accumulators of both CTAs' TMEM (two buffers of 256 columns: the epilogue of one tile overlaps
+// the MMAs of the next).  Warp 0: TMA producer; warp 1: TMEM allocation and (leader) MMA issue;
+// warps 4..7: epilogue.  No load uses cluster multicast; every wait is bounded.
+#include <cuda_bf16.h>
+
+#include "sc_codes.cuh"
+#include "sc_internal.h"
+#include "sc_ptx.cuh"
+
+namespace sc {
+namespace gemm_bf16 {
+
+constexpr int BM = 128;      // rows of x per CTA (256 per pair)
+constexpr int BN = 256;      // output columns per pair tile
+constexpr int BNH = BN / 2;  // weight columns each CTA loads
+constexpr int BK = 64;
+constexpr int kStages = 6;
+constexpr int kABytes = BM * BK * 2;
+constexpr int kBBytes = BNH * BK * 2;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kEpiWarp0 = 4, kEpiWarps = 4;
+constexpr uint32_t kTmemCols = 512;
+
+struct __align__(1024) Smem {
+  uint8_t a[kStages][kABytes];  // x tiles
+  uint8_t b[kStages][kBBytes];  // widened weight half-tiles
+  float sb[kEpiWarps][2][BN];   // per epilogue warp: the tile's scales and biases
+  uint64_t full[kStages];       // leader: both CTAs' operands of the stage landed
+  uint64_t empty[kStages];      // the pair's MMAs of the stage completed (leader's commit)
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];        // leader: both CTAs' epilogues
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+
+template <bool kF32Out>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                   const float* __restrict__ scales, const uint16_t* __restrict__ bias, void* __restrict__ y_out,
+                   int M, int N, int k_tiles, int m_tiles, int n_tiles, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int num_tiles = m_tiles * n_tiles;
+  volatile int* abort = &s.abort;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);   // the leader producer's arrive; the bytes of both CTAs
+      mbar_init(&s.empty[i], 1);  // the leader's commit
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 2 * kEpiWarps);
+    }
+    mbar_init(&s.drain, 1);
+    s.abort = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tm_x);
+    prefetch_tensormap(&tm_w);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&s.tmem_base, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_barrier();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (each CTA loads its own halves) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, last_parity = 0;
+      for (int tile = pair; tile < num_tiles && !*abort; tile += pairs) {
+        const int mt = tile % m_tiles, nt = tile / m_tiles;
+        const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM;
+        const int col0 = nt * BN + static_cast<int>(rank) * BNH;
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort, err, kSiteProducerEmpty)) break;
+          if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (kABytes + kBBytes));
+          const uint32_t bar = peer_addr(&s.full[stage], 0);
+          tma_load_2d_pair(s.a[stage], &tm_x, bar, kt * BK, row0);
+          tma_load_2d_pair(s.b[stage], &tm_w, bar, kt * BK, col0);
+          issued |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // The leader drains its own barriers; the peer's loads complete on the leader's barriers,
+      // which the leader's MMA has waited on before the pair's last commit.
+      if (leader)
+        for (int st = 0; st < kStages; ++st)
+          if (issued & (1u << st)) mbar_wait_drain(&s.full[st], (last_parity >> st) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA) ----------------
+    if (leader && lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(2 * BM, BN);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += pairs) {
+        if (!mbar_wait(&s.acc_empty[acc], acc_phase ^ 1u, abort, err, kSiteMmaAccum)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * BN);
+        bool ready = mbar_test_wait(&s.full[stage], phase);
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!ready && !mbar_poll(&s.full[stage], phase, abort, err, kSiteMmaInput)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int cur = stage;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          ready = kt + 1 < k_tiles && mbar_test_wait(&s.full[stage], phase);
+          const uint32_t a0 = smem_u32(s.a[cur]), b0 = smem_u32(s.b[cur]);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc_mma_f16_pair(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
+                            (kt | kk) != 0 ? 1u : 0u);
+          tc_commit_pair_both(&s.empty[cur], 0x3);
+        }
+        if (!ok) break;
+        tc_commit_pair_both(&s.acc_full[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      tc_commit_pair(peer_addr(&s.drain, 0));
+      mbar_wait_drain(&s.drain, 0);
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
+    // ---------------- epilogue (each CTA: its 128 rows x 256 columns) ----------------
+    const int ew = warp - kEpiWarp0;
+    float* s_scale = s.sb[ew][0];
+    float* s_bias = s.sb[ew][1];
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool vec_ok = (N % 8) == 0, vec4_ok = (N % 4) == 0;
+    for (int tile = pair; tile < num_tiles; tile += pairs) {
+      const int mt = tile % m_tiles, nt = tile / m_tiles;
+      const int n0 = nt * BN;
+      const int row = mt * 2 * BM + static_cast<int>(rank) * BM + ew * 32 + lane;
+      __syncwarp();
+      for (int c = lane; c < BN; c += 32) {
+        const int n = n0 + c;
+        s_scale[c] = scales[n];
+        s_bias[c] = (bias != nullptr && n < N) ? __uint_as_float(static_cast<uint32_t>(bias[n]) << 16) : 0.0f;
+      }
+      __syncwarp();
+      int ready = 0;
+      if (lane == 0) ready = mbar_wait(&s.acc_full[acc], acc_phase, abort, err, kSiteEpilogueFull) ? 1 : 0;
+      if (!__shfl_sync(0xFFFFFFFFu, ready, 0)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld_32(tbase + ch * 32, r);
+        tmem_wait_ld();
+        const int n = n0 + ch * 32;
+        if (kF32Out) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            r[j] = __float_as_uint(
+                __fadd_rn(__fmul_rn(__uint_as_float(r[j]), s_scale[ch * 32 + j]), s_bias[ch * 32 + j]));
+          if (row < M) {
+            float* dst = static_cast<float*>(y_out) + static_cast<int64_t>(row) * N + n;
+            if (vec4_ok && n + 32 <= N) {
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) d4[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n + j < N) dst[j] = __uint_as_float(r[j]);
+            }
+          }
+        } else {
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float v0 =
+                __fadd_rn(__fmul_rn(__uint_as_float(r[j]), s_scale[ch * 32 + j]), s_bias[ch * 32 + j]);
+            const float v1 = __fadd_rn(__fmul_rn(__uint_as_float(r[j + 1]), s_scale[ch * 32 + j + 1]),
+                                       s_bias[ch * 32 + j + 1]);
+            const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+            packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          if (row < M) {
+            uint16_t* dst = static_cast<uint16_t*>(y_out) + static_cast<int64_t>(row) * N + n;
+            if (vec_ok && n + 32 <= N) {
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                d4[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n + j < N) dst[j] = static_cast<uint16_t>(packed[j / 2] >> (16 * (j & 1)));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(peer_addr(&s.acc_empty[acc], 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  // Neither CTA leaves while the pair's MMAs, TMEM or barriers may still reach its memory.
+  __syncwarp();
+  tc_fence_before();
+  cluster_barrier();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
+// Widens the arena's codes [n_pad][k_pad] to bf16 in the same layout: 16 codes per thread and step,
+// four steps in flight per thread.
+template <int kKind, bool kNaN>
+__global__ void __launch_bounds__(256) widen_codes(const uint4* __restrict__ codes, uint4* __restrict__ out,
+                                                    int64_t chunks) {
+  constexpr int kUnroll = 4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + (kUnroll - 1) * stride < chunks; i += kUnroll * stride) {
+    uint4 in[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) in[u] = __ldcs(codes + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      uint4 lo, hi;
+      codes16_to_bf16<kKind, kNaN>(in[u], lo, hi);
+      out[2 * (i + u * stride)] = lo;
+      out[2 * (i + u * stride) + 1] = hi;
+    }
+  }
+  for (; i < chunks; i += stride) {
+    uint4 lo, hi;
+    codes16_to_bf16<kKind, kNaN>(__ldcs(codes + i), lo, hi);
+    out[2 * i] = lo;
+    out[2 * i + 1] = hi;
+  }
+}
+
+template <bool kF32Out>
+cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const sc_weight* w, const uint16_t* bias,
+                        void* y, int64_t m, int* err, int sm_count, cudaStream_t stream) {
+  auto kernel = gemm_bf16_pair<kF32Out>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const int m_tiles = static_cast<int>((m + 2 * BM - 1) / (2 * BM));
+  const int n_tiles = static_cast<int>(w->n_pad / BN);
+  const int k_tiles = static_cast<int>(w->k_pad / BK);
+  const int tiles = m_tiles * n_tiles;
+  const int max_pairs = sm_count / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias, y,
+                            static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err);
+}
+
+}  // namespace gemm_bf16
+
+size_t widened_bytes(const sc_weight* w) { return static_cast<size_t>(w->n_pad) * static_cast<size_t>(w->k_pad) * 2; }
+
+cudaError_t launch_widen(const sc_weight* w, void* out, int sm_count, cudaStream_t stream) {
+  const int64_t chunks = w->n_pad * w->k_pad / 16;
+  const int64_t want = (chunks + 255) / 256;
+  const int blocks = static_cast<int>(want < 8LL * sm_count ? want : 8LL * sm_count);
+  const uint4* codes = reinterpret_cast<const uint4*>(w->values);
+  uint4* dst = static_cast<uint4*>(out);
+  if (w->kind == SC_WEIGHT_INT8)
+    gemm_bf16::widen_codes<1, false><<<blocks, 256, 0, stream>>>(codes, dst, chunks);
+  else if (w->has_nan_codes)
+    gemm_bf16::widen_codes<2, true><<<blocks, 256, 0, stream>>>(codes, dst, chunks);
+  else
+    gemm_bf16::widen_codes<2, false><<<blocks, 256, 0, stream>>>(codes, dst, chunks);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_bf16(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
+                             const uint16_t* bias, void* y, bool f32_out, int64_t m, int* err, int sm_count,
+                             cudaStream_t stream) {
+  return f32_out ? gemm_bf16::launch_gemm<true>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream)
+                 : gemm_bf16::launch_gemm<false>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream);
+}
+
+}  // namespace sc

@@ -67,6 +67,17 @@ cudaError_t launch_gemm_pair(const CUtensorMap& tmap_x, const sc_weight* w, cons
 // Rows above which the CTA-pair GEMM takes over from the single-CTA one.
 constexpr int64_t kPairMinRows = 128;
 
+// The two-launch large-M route: the codes widened to bf16 [n_pad][k_pad] in the caller's workspace
+// (widened_bytes of it), then the pair GEMM on bf16 operands (tmap_w over the widened copy).  Taken
+// from kWidenMinRows rows, where converting the codes once beats converting them in every 256-row
+// block (measured on B200: even at 256..1024 rows, 10-20 % ahead from 2048).
+constexpr int64_t kWidenMinRows = 1536;
+size_t widened_bytes(const sc_weight* w);
+cudaError_t launch_widen(const sc_weight* w, void* out, int sm_count, cudaStream_t stream);
+cudaError_t launch_gemm_bf16(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
+                             const uint16_t* bias, void* y, bool f32_out, int64_t m, int* err, int sm_count,
+                             cudaStream_t stream);
+
 // CTA count and workspace of the skinny product.
 int gemv_splits(const sc_weight* w, int64_t m, int sm_count);
 size_t gemv_workspace_bytes(const sc_weight* w, int64_t m, int sm_count);

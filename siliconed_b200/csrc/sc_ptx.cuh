@@ -146,6 +146,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 2D tensor-map load into this CTA's shared memory for a CTA-pair MMA (.cta_group::2, no
+// multicast): the bytes are counted on the mbarrier at shared::cluster address `bar_cluster`, which
+// may be the leader CTA's, so one barrier sees both CTAs' operands land.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
 // 1D bulk copy global -> this CTA's shared memory, completing on `bar` (no multicast).  Both addresses
 // 16-byte aligned, `bytes` a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

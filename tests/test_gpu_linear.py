@@ -61,21 +61,24 @@ def rel_l2(got, ref) -> float:
     return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-300))
 
 
-def linear_ex(ctx, w, x_dev, m, bias_dev, f32: bool):
+def linear_ex(ctx, w, x_dev, m, bias_dev, f32: bool, workspace: bool = True):
+    """sc_linear_ex through ctypes, with a workspace of the reported size (workspace=True) or none
+    (for m > 128: the fused pair kernel instead of the widened route)."""
     out = torch.empty((m, w.n), dtype=torch.float32 if f32 else torch.bfloat16, device="cuda")
-    need = w.workspace_bytes(m)
-    ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    need = w.workspace_bytes(m) if workspace else 0
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda") if need else None
+    ws_ptr = ws.data_ptr() if ws is not None else 0
     st = torch.cuda.current_stream().cuda_stream
     status = ctx.lib.sc_linear_ex(ctx.ptr, w.ptr, ctypes.c_void_p(x_dev.data_ptr()), m,
                                   ctypes.c_void_p(bias_dev.data_ptr() if bias_dev is not None else 0),
                                   ctypes.c_void_p(out.data_ptr()), abi.OUT_F32 if f32 else abi.OUT_BF16,
-                                  ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.c_void_p(st))
+                                  ctypes.c_void_p(ws_ptr), need, ctypes.c_void_p(st))
     ctx.check(status)
     ctx.poll_errors()
     return out
 
 
-def check_against_oracle(ctx, kind, x_bits, codes_kn, s, bias_bits, label):
+def check_against_oracle(ctx, kind, x_bits, codes_kn, s, bias_bits, label, workspace=True):
     """Runs bf16 and fp32 outputs through the ABI and compares them with the oracle's route."""
     m, k = x_bits.shape
     n = codes_kn.shape[1]
@@ -87,14 +90,20 @@ def check_against_oracle(ctx, kind, x_bits, codes_kn, s, bias_bits, label):
     else:
         wf = oracle.dequantize(codes_kn, oracle.E4M3, s, oracle.SCALE_F32, oracle.LAYOUT_COLUMNS, n).reshape(k, n)
         c_ref, y_ref = oracle.linear_widened(x_bits, wf, bias_bits)
-    y32 = host(linear_ex(ctx, w, xd, m, bd, True))
+    y32 = host(linear_ex(ctx, w, xd, m, bd, True, workspace))
     e32 = rel_l2(y32, c_ref)
     assert e32 <= REL_L2_F32, f"{label}: fp32 rel-L2 {e32}"
-    y16 = bf16_host(linear_ex(ctx, w, xd, m, bd, False))
+    y16 = bf16_host(linear_ex(ctx, w, xd, m, bd, False, workspace))
     yf, rf = f32_of_bf16(y16), f32_of_bf16(y_ref)
     e16, mx = rel_l2(yf, rf), float(np.max(np.abs(yf.astype(np.float64) - rf)))
     assert e16 <= REL_L2_BF16 and mx <= MAX_ABS_BF16, f"{label}: bf16 rel-L2 {e16}, max-abs {mx}"
-    excess = np.abs(yf.astype(np.float64) - c_ref) - (2.0 ** -7 * np.abs(c_ref) + 1e-6)
+    # One bf16 ulp of the value, plus the spread that a change of fp32 summation order can make:
+    # 8 sqrt(K) 2^-24 sqrt(sum_k (x w)^2), a loose multiple of its typical size.
+    wf = oracle.dequantize(codes_kn, kind, s, oracle.SCALE_F32, oracle.LAYOUT_COLUMNS, n).reshape(k, n)
+    xf = torch.from_numpy(f32_of_bf16(x_bits))
+    spread = torch.sqrt((xf * xf) @ torch.from_numpy(wf * wf)).numpy().astype(np.float64)
+    bound = 2.0 ** -7 * np.abs(c_ref) + 8.0 * np.sqrt(k) * 2.0 ** -24 * spread + 1e-9
+    excess = np.abs(yf.astype(np.float64) - c_ref) - bound
     assert float(excess.max()) <= 0.0, f"{label}: more than one bf16 ulp from the fp32 result"
     w.close()
     return e32, e16
@@ -301,6 +310,101 @@ def test_errors_are_statuses(ctx):
     assert e.value.status == abi.UNSUPPORTED_SHAPE
     w.close()
     ctx.poll_errors()                                   # no device-side wait gave up
+
+
+# ---------------------------------------------------------------------------------------------
+# more shapes of the pair GEMM (fewer tiles than CTA pairs, ragged m and n, short K), and batch
+# invariance: every output is summed in the same order whatever tile it falls in
+
+
+@pytest.mark.parametrize("kind,m,k,n", [(abi.WEIGHT_INT8, 256, 3072, 3072), (abi.WEIGHT_INT8, 600, 4096, 1000),
+                                        (abi.WEIGHT_INT8, 4096, 512, 3072), (abi.WEIGHT_E4M3, 384, 2048, 2560),
+                                        (abi.WEIGHT_INT8, 2304, 256, 5000), (abi.WEIGHT_E4M3, 1600, 1024, 1000)])
+def test_linear_more_shapes_match_oracle(ctx, kind, m, k, n):
+    g = np.random.default_rng(m + k + n)
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    # Scales keep |y| below 4, where the max-abs bar of 2e-2 exceeds one bf16 ulp.
+    amp = 0.02 * np.sqrt(768.0 / k)
+    if kind == abi.WEIGHT_INT8:
+        q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+        s = (np.abs(g.standard_normal(n)) * amp / 127 + 1e-7).astype(np.float32)
+    else:
+        q = configs.to_e4m3_codes(g.standard_normal((k, n), dtype=np.float32) * 4)
+        q[(q & 0x7F) == 0x7F] ^= 1
+        s = (np.abs(g.standard_normal(n)) * amp / 448 + 1e-7).astype(np.float32)
+    b = configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.01)
+    check_against_oracle(ctx, kind, x, q, s, b, f"shape {m}x{k}x{n}")
+
+
+@pytest.mark.parametrize("kind,m,k,n", [(abi.WEIGHT_INT8, 600, 4096, 1000), (abi.WEIGHT_E4M3, 384, 2048, 2560)])
+def test_fused_pair_kernel_matches_oracle(ctx, kind, m, k, n):
+    """The fused pair kernel (no workspace: codes converted in shared memory) on its own."""
+    g = np.random.default_rng(m * 3 + n)
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    amp = 0.02 * np.sqrt(768.0 / k)
+    if kind == abi.WEIGHT_INT8:
+        q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+        s = (np.abs(g.standard_normal(n)) * amp / 127 + 1e-7).astype(np.float32)
+    else:
+        q = configs.to_e4m3_codes(g.standard_normal((k, n), dtype=np.float32) * 4)
+        q[(q & 0x7F) == 0x7F] ^= 1
+        s = (np.abs(g.standard_normal(n)) * amp / 448 + 1e-7).astype(np.float32)
+    b = configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.01)
+    check_against_oracle(ctx, kind, x, q, s, b, f"fused {m}x{k}x{n}", workspace=False)
+
+
+@pytest.mark.parametrize("kind,m,k,n,nan", [(abi.WEIGHT_INT8, 1536, 3072, 3072, False),
+                                            (abi.WEIGHT_INT8, 4096, 512, 3072, False),
+                                            (abi.WEIGHT_E4M3, 2000, 2048, 2560, False),
+                                            (abi.WEIGHT_E4M3, 1600, 512, 700, True)])
+def test_widened_and_fused_routes_agree(ctx, kind, m, k, n, nan):
+    """The widened route (from 1536 rows, workspace given) and the fused kernel (none) give the
+    same bits."""
+    g = np.random.default_rng(m + 7 * k + n)
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    if kind == abi.WEIGHT_INT8:
+        q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+    else:
+        q = configs.to_e4m3_codes(g.standard_normal((k, n), dtype=np.float32) * 4)
+        q[(q & 0x7F) == 0x7F] ^= 1
+        if nan:
+            q[g.integers(0, k, 20), g.integers(0, n, 20)] = 0x7F
+    s = (np.abs(g.standard_normal(n)) * 1e-3 + 1e-6).astype(np.float32)
+    w = QuantizedWeight(ctx, q, kind, s)
+    n_pad, k_pad = -(-n // 256) * 256, -(-k // 64) * 64
+    assert w.workspace_bytes(m) == n_pad * k_pad * 2 and w.workspace_bytes(1535) == 0
+    xd = bf16_dev(x)
+    bd = bf16_dev(configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.01))
+    for f32 in (True, False):
+        got = [linear_ex(ctx, w, xd, m, bd, f32, ws) for ws in (True, False)]
+        if f32:
+            vals = [host(t) for t in got]
+            bits = [v.view(np.uint32) for v in vals]
+        else:
+            bits = [bf16_host(t) for t in got]
+            vals = [f32_of_bf16(b) for b in bits]
+        nans = [np.isnan(v) for v in vals]
+        assert np.array_equal(nans[0], nans[1]), f"NaN positions differ (f32={f32})"
+        assert nan or not nans[0].any()
+        assert np.array_equal(bits[0][~nans[0]], bits[1][~nans[1]]), f"routes differ (f32={f32})"
+    w.close()
+
+
+def test_rows_do_not_depend_on_the_batch(ctx):
+    """Rows computed at different offsets in a tile and in batches of different sizes come out bit
+    for bit the same."""
+    g = np.random.default_rng(11)
+    m, k, n = 4096, 3072, 3072
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+    s = (np.abs(g.standard_normal(n)) * 0.02 / 127 + 1e-6).astype(np.float32)
+    w = QuantizedWeight(ctx, q, abi.WEIGHT_INT8, s)
+    xd = bf16_dev(x)
+    full = host(linear_ex(ctx, w, xd, m, None, True))
+    for r0, rows in ((0, 256), (3584, 512), (1000, 600), (2048, 130)):
+        part = host(linear_ex(ctx, w, xd[r0:r0 + rows].contiguous(), rows, None, True))
+        assert np.array_equal(part.view(np.uint32), full[r0:r0 + rows].view(np.uint32)), (r0, rows)
+    w.close()
 
 
 # ---------------------------------------------------------------------------------------------
