@@ -151,6 +151,19 @@ SC_API sc_status sc_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, in
 SC_API sc_status sc_linear_ex(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, void* y,
                               sc_out_type y_type, void* workspace, size_t workspace_bytes, void* stream);
 
+/* sc_linear_ex with its scratch in a 32 MiB device array of the library instead of a workspace: it
+ * allocates nothing and takes no workspace argument.  No counterpart in the reference: it serves
+ * callers that have no scratch buffer to pass (a binding that keeps the signature of
+ * WeightProducts.linear, which carries only a, c, m, k, n) and may not allocate per call
+ * (cudaMalloc / cudaFree synchronise the device, which a serving loop cannot afford).  A product
+ * whose sc_workspace_size exceeds 32 MiB (from 1536 rows: n_pad * k_pad * 2 bytes of widened weight)
+ * returns SC_UNSUPPORTED_SHAPE.  The first call on a device sets up the array's address
+ * (cudaGetSymbolAddress) and should come before any stream capture.  All calls on a device share the
+ * array and leave the last call's contents in it (nothing in it needs to start at zero); calls that
+ * overlap on the GPU race on it. */
+SC_API sc_status sc_linear_ex_noalloc(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m,
+                                      const sc_bf16* bias, void* y, sc_out_type y_type, void* stream);
+
 /* sc_linear for an int8 weight (SC_INVALID_ARG on another kind). */
 SC_API sc_status sc_linear_w8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
                        void* workspace, size_t workspace_bytes, void* stream);

@@ -45,6 +45,7 @@ SIGNATURES = {
     "sc_workspace_size": (_I, [_P, _P, _I64, ctypes.POINTER(_SZ)]),
     "sc_linear": (_I, [_P, _P, _P, _I64, _P, _P, _P, _SZ, _P]),
     "sc_linear_ex": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _SZ, _P]),
+    "sc_linear_ex_noalloc": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P]),
     "sc_linear_w8": (_I, [_P, _P, _P, _I64, _P, _P, _P, _SZ, _P]),
     "sc_linear_fp8": (_I, [_P, _P, _P, _I64, _P, _P, _P, _SZ, _P]),
     "sc_gemv_w8": (_I, [_P, _P, _P, _I64, _P, _P, _P, _SZ, _P]),
