@@ -139,9 +139,10 @@ def route_kernels(case, ws_bytes: int) -> list[str]:
     return ["gemm_w8_pair"]
 
 
-def cpu_baseline(case, budget_s: float = 12.0):
+def cpu_baseline(case, budget_s: float = 12.0, steps: int | None = None, warmup: int = 0):
     """The reference's CPU path restated (the oracle): dequantize W (OpenMP, all host threads), then
-    an fp32 GEMM on the CPU (torch.matmul, all threads), on a bounded sample of the rows."""
+    an fp32 GEMM on the CPU (torch.matmul, all threads), on a bounded sample of the rows.  Timed
+    repetitions run until `budget_s` (at most 1000), or exactly `steps` after `warmup` untimed ones."""
     import torch
     import oracle
     threads = os.cpu_count() or 1
@@ -152,15 +153,20 @@ def cpu_baseline(case, budget_s: float = 12.0):
     x = torch.from_numpy(((case.x[:rows].astype(np.uint32) << 16).view(np.float32)).copy())
     bias = None if case.bias is None else torch.from_numpy((case.bias.astype(np.uint32) << 16).view(np.float32))
     reps, t_total = 0, 0.0
-    while reps == 0 or (t_total < budget_s and reps < 1000):
+    for i in range(-warmup, 10 ** 9):
+        if steps is not None and reps >= steps:
+            break
+        if steps is None and reps > 0 and (t_total >= budget_s or reps >= 1000):
+            break
         t0 = time.perf_counter()
         w = oracle.dequantize(codes_kn, case.kind, case.scales, oracle.SCALE_F32, oracle.LAYOUT_COLUMNS,
                               case.n).reshape(case.k, case.n)
         y = x @ torch.from_numpy(w)
         if bias is not None:
             y += bias
-        t_total += time.perf_counter() - t0
-        reps += 1
+        if i >= 0:
+            t_total += time.perf_counter() - t0
+            reps += 1
     per = t_total / reps
     flops = 2.0 * rows * case.k * case.n
     byts = rows * case.k * 2 + case.n * case.k + case.n * 4 + rows * case.n * 2
@@ -174,12 +180,10 @@ def run_reference(args):
         return 0
     case = make_case(args.workload)
     metric, unit = metric_of(case)
-    for _ in range(max(args.warmup, 0) and 1):
-        cpu_baseline(case, budget_s=0.0)
-    per, flops, byts, threads, rows, reps = cpu_baseline(case, budget_s=max(1.0, 2.0 * args.steps))
+    per, flops, byts, threads, rows, reps = cpu_baseline(case, steps=max(args.steps, 1), warmup=max(args.warmup, 0))
     value = (byts / per / 1e9) if unit == "GB/s" else (flops / per / 1e12)
-    sample = (f"{rows} of {case.m} rows per step ({reps} steps timed), full weight dequantized each step "
-              f"(oracle/ C, OpenMP) + fp32 torch.matmul on the CPU")
+    sample = (f"{rows} of {case.m} rows per step ({reps} steps timed after {args.warmup} untimed), full weight "
+              f"dequantized each step (oracle/ C, OpenMP) + fp32 torch.matmul on the CPU")
     line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
             "steps": reps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -307,7 +311,7 @@ def run_ours(args):
                         "path": "QuantizedWeight.linear (sc_linear) with pinned host x / y copied in the timed region"},
                 "gpu_launches": args.steps * len(route_kernels(case, ws_bytes)),
                 "step_ms_min": min(per_step), "step_ms_median": statistics.median(per_step)}
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             per, flops, byts, threads, rows, reps = cpu_baseline(case)
             cv = (byts / per / 1e9) if unit == "GB/s" else (flops / per / 1e12)
             line["cpu_baseline"] = {"value": cv, "unit": unit, "cores": threads, "kind": "port",
