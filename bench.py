@@ -11,7 +11,8 @@ With N > 1 (one process per GPU under torch.distributed.run) every rank runs its
 workload with the weight replicated (batch sharding: the images / token batches are independent, no
 collective on the data path); ``value`` is the work of all ranks over the slowest rank's time.
 Timing: W untimed warm-up steps, then K timed steps, each bracketed by CUDA events on the launching
-stream, with the L2 flushed (a 256 MiB write) before every step; barrier + synchronize around the
+stream, with the L2 flushed (a 256 MiB write, then a 256 MiB read of another buffer so that the L2
+holds clean lines) before every step; barrier + synchronize around the
 timed region; the max over ranks.
 """
 from __future__ import annotations
@@ -60,7 +61,7 @@ def describe(case, workload):
     return {"workload": f"{workload}: {case.name} x bf16 [{case.m}, {case.k}] . W [{case.k}, {case.n}] "
                         f"{'int8' if case.kind == 1 else 'e4m3'} per-channel, fp32 accumulate, bf16 out",
             "m": case.m, "k": case.k, "n": case.n, "bias": case.bias is not None, "bound": bound,
-            "l2": "flushed before every timed step (256 MiB write)"}
+            "l2": "flushed before every timed step (256 MiB write, then a 256 MiB read that leaves the L2 clean)"}
 
 
 def metric_of(case):
@@ -217,13 +218,22 @@ def run_ours(args):
     ws_bytes = w.workspace_bytes(case.m)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    clean = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
+
+    def flush_l2(i):
+        # A write larger than the L2 evicts the inputs; a read of another buffer larger than the L2 then
+        # replaces the written (dirty) lines with clean ones, so that their write-back does not land in
+        # the next timed step.
+        flush.fill_(i & 0xFF)
+        torch.sum(clean, dim=0, out=sink)
     stream = torch.cuda.current_stream()
 
     def step():
         w.linear(x, bias=bias, out=y, workspace=ws, stream=stream)
 
     for _ in range(args.warmup):
-        flush.fill_(1)
+        flush_l2(1)
         step()
     ctx.poll_errors()
 
@@ -238,7 +248,7 @@ def run_ours(args):
         # figure below measures the public call itself).
         torch.cuda._sleep(int(2e6) * max(1, args.steps // 10))
         for i in range(args.steps):
-            flush.fill_(i & 0xFF)
+            flush_l2(i)
             starts[i].record(stream)
             step()
             ends[i].record(stream)
@@ -325,6 +335,221 @@ def run_ours(args):
     return 0
 
 
+DIT_WORKLOADS = ("cfg3", "cfg5")
+
+
+def dit_cpu_seconds(shapes, rows_full: int, rows_sample: int = 256):
+    """The reference's CPU route for one block's linears (oracle dequantization of each weight, C with
+    OpenMP over all host threads, then an fp32 torch.matmul), timed on `rows_sample` rows and scaled
+    to `rows_full`; returns (seconds per block, threads)."""
+    import torch
+    import oracle
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    torch.set_num_threads(threads)
+    rng = np.random.default_rng(0)
+    total = 0.0
+    for k, n in shapes:
+        q = rng.integers(-127, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+        sc = np.full(n, 1e-3, np.float32)
+        x = torch.randn(rows_sample, k)
+        t0 = time.perf_counter()
+        w = oracle.dequantize(q, 1, sc, oracle.SCALE_F32, oracle.LAYOUT_COLUMNS, n).reshape(k, n)
+        t1 = time.perf_counter()
+        x @ torch.from_numpy(w)
+        t2 = time.perf_counter()
+        total += (t1 - t0) + (t2 - t1) * rows_full / rows_sample
+    return total, threads
+
+
+def run_dit(args):
+    """Configs 3 and 5 (the DiT block and the 8-step MMDiT denoise) over the quantized linears.
+
+    cfg3: a step is one forward of one single-stream block (S = 4096 image + 512 text tokens, d 3840);
+    metric TFLOP/s of its linears and attention.  cfg5: a step is one denoise step (one forward of the
+    60-block MMDiT over the batch); the batch of 8 images is split across the ranks (strong scaling);
+    metric s/image of the 8-step denoise = 8 x (slowest rank's time per step) / 8 images."""
+    import torch
+    import torch.distributed as dist
+    from siliconed_b200 import dit
+    from siliconed_b200.products import Context
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    ctx = Context(local)
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    if args.workload == "cfg3":
+        s_img, s_txt, d = 4096, 512, 3840
+        s = s_img + s_txt
+        model = dit.ZImageBlock(ctx, dim=d, heads=30, hidden=10240, seed=0)
+        x0 = torch.randn(s, d, generator=g, device="cuda")
+        x = x0.clone()
+        grid = int(round(s_img ** 0.5))
+        freqs = dit.rope_table(dit.image_text_positions(s_txt, grid)).cuda()
+        adaln = dit.timestep_embedding(0.5)
+        flops = model.flops(s)
+
+        def step(i):
+            x.copy_(x0)
+            model.forward(x, freqs, adaln)
+        images = None
+        metric, unit, hib = "DiT block (config 3) TFLOP/s", "TFLOP/s", True
+        launches_per_step = 15
+        cpu_shapes = [(d, 3 * d), (d, d), (d, 2 * 10240), (10240, d), (256, 4 * d)]
+        cpu_rows = s
+        config = {"workload": "cfg3: one single-stream DiT block, 4096 image + 512 text tokens, d 3840, 30 x 128 heads, "
+                              "SwiGLU 10240, adaLN 256 -> 4 d; int8 per-channel linears (N(0, 0.02) random init)",
+                  "tokens": s, "dim": d, "heads": 30, "hidden": 10240, "batch": 1}
+    else:
+        batch_total, st, si, d = 8, 256, 4096, 3072
+        if batch_total % world != 0:
+            raise SystemExit(f"cfg5: {world} ranks do not divide the batch of {batch_total}")
+        batch = batch_total // world
+        blocks = int(os.environ.get("SC_MMDIT_BLOCKS", "60"))
+        model = dit.MMDiT(ctx, blocks=blocks, dim=d, heads=24, mlp=12288, seed=0)
+        z = torch.randn(batch * si, 64, generator=g, device="cuda")
+        txt = (torch.randn(batch * st, d, generator=g, device="cuda")).to(torch.bfloat16)
+        freqs = dit.rope_table(dit.image_text_positions(st, 64)).cuda()
+        sig = torch.linspace(1.0, 0.0, 9).tolist()
+
+        def step(i):
+            v = model.forward(z, txt, batch, sig[i % 8], freqs)
+            z.add_(v, alpha=sig[i % 8 + 1] - sig[i % 8])
+        flops = model.flops_per_step(batch, st, si)
+        images = batch_total
+        metric, unit, hib = "DiT s/image 1024x1024 8-step (MMDiT, 60 double-stream blocks, batch 8)", "s/image", False
+        launches_per_step = None
+        cpu_shapes = [(256, 6 * d), (d, 3 * d), (d, d), (d, 12288), (12288, d)]
+        cpu_rows = batch_total * (st + si)
+        config = {"workload": f"cfg5: {blocks} double-stream MMDiT blocks, d 3072, 24 x 128 heads, MLP 12288 GELU (tanh), "
+                              f"4096 image + 256 text tokens, batch 8 ({batch} per rank), 8 Euler steps; int8 per-channel "
+                              f"linears (N(0, 0.02) random init), {model.weight_bytes() / 1e9:.1f} GB of weights per GPU",
+                  "blocks": blocks, "dim": d, "heads": 24, "mlp": 12288, "batch": batch_total, "batch_per_rank": batch,
+                  "steps_per_image": 8}
+
+    for i in range(args.warmup):
+        flush.fill_(1)
+        step(i)
+    torch.cuda.synchronize()
+    ctx.poll_errors()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            starts[i].record()
+            step(i)
+            ends[i].record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ctx.poll_errors()
+    per_step = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    t = torch.tensor([sum(per_step)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t.item()) / args.steps
+    tflops_rank = flops / (ms_per_step / 1e3) / 1e12
+    if images is None:
+        value = world * tflops_rank
+    else:
+        value = 8 * ms_per_step / 1e3 / images  # 8 steps of the whole batch, per image
+
+    # End to end through the public call: latents / activations from pinned host memory, the result back.
+    if args.workload == "cfg3":
+        host_in = x0.cpu().pin_memory()
+        host_out = torch.empty_like(host_in).pin_memory()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        x.copy_(host_in, non_blocking=True)
+        model.forward(x, freqs, adaln)
+        host_out.copy_(x, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        te = e0.elapsed_time(e1)
+        e2e = {"value": world * flops / (te / 1e3) / 1e12, "unit": unit, "h2d_bytes_per_step": host_in.numel() * 4,
+               "d2h_bytes_per_step": host_in.numel() * 4, "path": "ZImageBlock.forward with x from pinned host memory"}
+    else:
+        z_host = z.cpu().pin_memory()
+        t_host = txt.cpu().pin_memory()
+        out_host = torch.empty_like(z_host).pin_memory()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        z.copy_(z_host, non_blocking=True)
+        txt.copy_(t_host, non_blocking=True)
+        model.denoise(z, txt, batch, 8, freqs)
+        out_host.copy_(z, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": float(te.item()) / 1e3 / images, "unit": unit,
+               "h2d_bytes_per_step": (z_host.numel() * 4 + t_host.numel() * 2) // 8,
+               "d2h_bytes_per_step": z_host.numel() * 4 // 8,
+               "path": "MMDiT.denoise (8 steps) with latents and text from pinned host memory, latents back"}
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": hib,
+                "scaling": "strong" if images is not None else "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (random-init weights of the architecture, N(0,1) latents and activations)",
+                "config": config,
+                "roofline": {"bound": "tensor", "achieved": tflops_rank, "peak": peaks["bf16_tflops_sustained"],
+                             "unit": "TFLOP/s", "frac": tflops_rank / peaks["bf16_tflops_sustained"], "traffic": None,
+                             "peak_source": f"{peak_src} (sustained figure: a long step)",
+                             "note": "achieved = the step's linear and attention FLOPs per rank over the step's time"},
+                "clocks": clocks.summary(), "e2e": e2e,
+                "gpu_launches": (args.steps * launches_per_step if launches_per_step else None),
+                "step_ms_min": min(per_step), "step_ms_median": statistics.median(per_step)}
+        if images is not None:
+            line["gpu_launches"] = args.steps * dit_launches_per_step(model)
+        if not args.no_cpu_baseline and world == 1:
+            per_block, threads = dit_cpu_seconds(cpu_shapes, cpu_rows)
+            if images is None:
+                cv = flops / per_block / 1e12
+                sample = "one block's linears: 256 of 4608 rows timed, scaled to 4608 (attention not included)"
+            else:
+                per_block *= 2  # two streams
+                cv = per_block * len(model.blocks) * 8 / images
+                sample = ("one double-stream block's linears (both streams) on 256 of 34816 rows, scaled to the batch, "
+                          "x 60 blocks x 8 steps / 8 images (extrapolated; attention not included)")
+            line["cpu_baseline"] = {"value": cv, "unit": unit, "cores": threads, "kind": "port", "sample": sample}
+        print(json.dumps(line), flush=True)
+    model.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def dit_launches_per_step(model) -> int:
+    """This project's kernels in one MMDiT forward (the attention is the CUDA library's and not counted):
+    per stream and block the modulation GEMV, two LayerNorms, QK-norm + RoPE, GELU, two residuals and
+    four products (two launches each where the widened route runs, i.e. from 1536 rows)."""
+    blocks = len(model.blocks)
+    b = model._bufs[0] if model._bufs else None
+    batch, st, si = b if b else (8, 256, 4096)
+    def prod(m):
+        return 2 if m >= 1536 else 1
+    per_stream = lambda m: 1 + 2 + 1 + 1 + 2 + 4 * prod(m)
+    return blocks * (per_stream(batch * st) + per_stream(batch * si)) + prod(batch * si) * 2 + prod(batch * st) + 2
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -336,6 +561,14 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    if args.workload in DIT_WORKLOADS:
+        if args.impl == "reference":
+            rank = int(os.environ.get("RANK", "0"))
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the DiT workloads' reference arm is the "
+                                  "CPU extrapolation reported as cpu_baseline on the ours line"}), flush=True)
+            return 0
+        return run_dit(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -48,6 +48,15 @@ class Context:
         if status != abi.OK:
             raise SiliconedError(status, f"sc_ctx_create({device})")
         self.ptr = p
+        self._workspace = None
+
+    def workspace(self, nbytes: int, device) -> "torch.Tensor":
+        """The context's shared product workspace, at least ``nbytes`` long (grown on demand).  Products
+        that run concurrently on different streams need workspaces of their own (pass ``workspace=``);
+        calls on one stream may share this one."""
+        if self._workspace is None or self._workspace.numel() < nbytes:
+            self._workspace = torch.empty(int(nbytes), dtype=torch.uint8, device=device)
+        return self._workspace
 
     def close(self) -> None:
         if getattr(self, "ptr", None):
@@ -171,11 +180,27 @@ class QuantizedWeight:
             out = torch.empty((m, self.n), dtype=torch.bfloat16, device=x.device)
         need = self.workspace_bytes(m)
         if need and workspace is None:
-            workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+            workspace = self.ctx.workspace(need, x.device)
         ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
         fn = getattr(self.ctx.lib, fn_name)
         self.ctx.check(fn(self.ctx.ptr, self.ptr, _ptr(x), m, _ptr(bias), _ptr(out), _ptr(workspace), ws_bytes,
                           _stream_ptr(stream)))
+        return out
+
+    def linear_ex(self, x, out, bias=None, workspace=None, stream=None):
+        """sc_linear_ex: y = (x . q) * s + bias into `out`, bf16 or fp32 [M, N] (the output's dtype chooses)."""
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.shape[1] != self.k:
+            raise SiliconedError(abi.INVALID_ARG, f"x must be a CUDA bf16 [M, {self.k}] tensor")
+        m = x.shape[0]
+        if out.dtype not in (torch.bfloat16, torch.float32) or tuple(out.shape) != (m, self.n) or not out.is_contiguous():
+            raise SiliconedError(abi.INVALID_ARG, f"out must be a contiguous bf16 or fp32 [{m}, {self.n}] tensor")
+        need = self.workspace_bytes(m)
+        if need and workspace is None:
+            workspace = self.ctx.workspace(need, x.device)
+        ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        y_type = abi.OUT_F32 if out.dtype == torch.float32 else abi.OUT_BF16
+        self.ctx.check(self.ctx.lib.sc_linear_ex(self.ctx.ptr, self.ptr, _ptr(x), m, _ptr(bias), _ptr(out), y_type,
+                                                 _ptr(workspace), ws_bytes, _stream_ptr(stream)))
         return out
 
     def linear(self, x, bias=None, out=None, workspace=None, stream=None):
