@@ -335,6 +335,95 @@ def run_ours(args):
     return 0
 
 
+def run_colpar(args):
+    """cfg1-colpar: config 1 with the weight's columns split over the ranks (sc_weight_create_shard), every
+    rank multiplying the whole x by its columns, then one NCCL all-gather assembling y [M, N] on every rank.
+    value: the whole product's TFLOP/s with the gather (the slowest rank's time); the line also carries the
+    rate without it (strong scaling: the total work is fixed)."""
+    import torch
+    import torch.distributed as dist
+    from siliconed_b200 import configs, parallel
+    from siliconed_b200.products import Context, QuantizedWeight
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    case = configs.config1()
+    ranges = parallel.column_ranges(case.n, world)
+    n0, n1 = ranges[rank]
+    ctx = Context(local)
+    w = QuantizedWeight(ctx, case.codes_nk, case.kind, case.scales, published_nk=True, columns=(n0, n1))
+    x = torch.from_numpy(case.x.view(np.int16)).cuda().view(torch.bfloat16)
+    bias = torch.from_numpy(case.bias.view(np.int16)).cuda().view(torch.bfloat16)[n0:n1].contiguous()
+    y_local = torch.empty((case.m, n1 - n0), dtype=torch.bfloat16, device="cuda")
+    ws = torch.empty(max(w.workspace_bytes(case.m), 1), dtype=torch.uint8, device="cuda")
+    width = max(b - a for a, b in ranges)
+    blocks = torch.empty((world * case.m, width), dtype=torch.bfloat16, device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    def product():
+        w.linear(x, bias=bias, out=y_local, workspace=ws)
+
+    def gather():
+        if world > 1:
+            dist.all_gather_into_tensor(blocks, y_local if y_local.shape[1] == width else
+                                        torch.nn.functional.pad(y_local, (0, width - y_local.shape[1])))
+
+    def timed(fn_list):
+        for i in range(args.warmup):
+            flush.fill_(1)
+            for fn in fn_list:
+                fn()
+        st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            st[i].record()
+            for fn in fn_list:
+                fn()
+            en[i].record()
+        torch.cuda.synchronize()
+        t = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(st, en)) / args.steps], dtype=torch.float64,
+                         device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with ClockSampler(local) as clocks:
+        ms_gather = timed([product, gather])
+        ms_local = timed([product])
+    ctx.poll_errors()
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        value = case.flops / (ms_gather / 1e3) / 1e12
+        line = {"metric": "int8-weight GEMM TFLOP/s at M=4096 (column-parallel, with the all-gather)", "value": value,
+                "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": ms_gather, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "cfg1-colpar: config 1, W's columns split over the ranks, y all-gathered (NCCL)",
+                           "m": case.m, "k": case.k, "n": case.n, "columns_per_rank": width,
+                           "parallelism": f"column-parallel x{world}"},
+                "without_gather": {"value": case.flops / (ms_local / 1e3) / 1e12, "ms_per_step": ms_local},
+                "gather_bytes_per_rank": int(case.m * width * 2 * (world - 1)),
+                "roofline": {"bound": "tensor", "achieved": value / world, "peak": peaks["bf16_tflops"],
+                             "unit": "TFLOP/s", "frac": value / world / peaks["bf16_tflops"], "traffic": None,
+                             "peak_source": peak_src},
+                "clocks": clocks.summary(), "gpu_launches": args.steps * (2 if case.m >= 1536 else 1)}
+        print(json.dumps(line), flush=True)
+    w.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 DIT_WORKLOADS = ("cfg3", "cfg5")
 
 
@@ -561,6 +650,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    if args.workload == "cfg1-colpar" and args.impl == "ours":
+        return run_colpar(args)
     if args.workload in DIT_WORKLOADS:
         if args.impl == "reference":
             rank = int(os.environ.get("RANK", "0"))
