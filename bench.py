@@ -396,9 +396,16 @@ def run_colpar(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    fused = None
+    if world > 1:
+        fused = parallel.FusedColumnParallelLinear(ctx, case.codes_nk, case.kind, case.scales, case.n, case.m,
+                                                   published_nk=True,
+                                                   bias=torch.from_numpy(case.bias.view(np.int16)).cuda()
+                                                   .view(torch.bfloat16))
     with ClockSampler(local) as clocks:
         ms_gather = timed([product, gather])
         ms_local = timed([product])
+        ms_fused = timed([lambda: fused(x)]) if fused is not None else None
     ctx.poll_errors()
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -411,12 +418,18 @@ def run_colpar(args):
                            "m": case.m, "k": case.k, "n": case.n, "columns_per_rank": width,
                            "parallelism": f"column-parallel x{world}"},
                 "without_gather": {"value": case.flops / (ms_local / 1e3) / 1e12, "ms_per_step": ms_local},
+                "fused_gather": (None if ms_fused is None else
+                                 {"value": case.flops / (ms_fused / 1e3) / 1e12, "ms_per_step": ms_fused,
+                                  "path": "sc_linear_allgather (product epilogue stores every tile to every rank "
+                                          "over NVLink) + sc_allgather_wait"}),
                 "gather_bytes_per_rank": int(case.m * width * 2 * (world - 1)),
                 "roofline": {"bound": "tensor", "achieved": value / world, "peak": peaks["bf16_tflops"],
                              "unit": "TFLOP/s", "frac": value / world / peaks["bf16_tflops"], "traffic": None,
                              "peak_source": peak_src},
                 "clocks": clocks.summary(), "gpu_launches": args.steps * (2 if case.m >= 1536 else 1)}
         print(json.dumps(line), flush=True)
+    if fused is not None:
+        fused.close()
     w.close()
     ctx.close()
     if world > 1:

@@ -181,6 +181,35 @@ SC_API sc_status sc_linear_fp8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x
 SC_API sc_status sc_gemv_w8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- several GPUs: the fused column-parallel gather ---------------------------------------- */
+
+/*
+ * No counterpart in the reference (it has no multi-device code): the column-parallel linear of one
+ * process per GPU, with the all-gather of y fused into the product.  `w` holds this rank's columns
+ * [col0, col0 + n) of an [K, n_total] weight (sc_weight_create_shard); every rank multiplies the same
+ * x [m, K].  The product (widened route: `workspace` of n_pad * k_pad * 2 bytes, as sc_workspace_size
+ * reports from 1536 rows, is required at every m) stores each bf16 output tile straight into the
+ * output y_peers[r] [m, n_total] of every rank r over NVLink (peer stores: the pointers come from
+ * sc_ipc_open; y_peers[rank] is this rank's own), then raises flag_peers[r][rank] = epoch on every
+ * rank.  All ranks call it with the same epoch, which starts at 1 and grows by one per call; the
+ * flags [world] uint32 start at zero.  sc_allgather_wait(flags of this rank) then holds this rank's
+ * stream until every rank's columns have landed (bounded: SC_TIMEOUT through sc_poll_errors).  The
+ * outputs must be double-buffered across consecutive calls (a rank may start call e + 1 while another
+ * still reads the result of call e).  world <= 8; col0 and n_total multiples of 8.
+ */
+SC_API sc_status sc_linear_allgather(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
+                                     void* const* y_peers, uint32_t* const* flag_peers, int world, int rank,
+                                     int64_t col0, int64_t n_total, uint32_t epoch, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+SC_API sc_status sc_allgather_wait(sc_ctx* ctx, const uint32_t* flags, int world, uint32_t epoch, void* stream);
+
+/* CUDA IPC plumbing for the peer pointers (no counterpart in the reference): the 64-byte handle of the
+ * device allocation holding device_ptr in this process and device_ptr's offset in it; the same address
+ * mapped in another process (peer access enabled); the unmap (the pointer and offset sc_ipc_open took). */
+SC_API sc_status sc_ipc_handle(sc_ctx* ctx, void* device_ptr, void* handle_out, size_t* offset_out);
+SC_API sc_status sc_ipc_open(sc_ctx* ctx, const void* handle, size_t offset, void** device_ptr_out);
+SC_API sc_status sc_ipc_close(sc_ctx* ctx, void* device_ptr, size_t offset);
+
 /* ---- synchronisation and device-side errors ----------------------------------------------- */
 
 /* Waits for `stream`. */

@@ -46,6 +46,11 @@ SIGNATURES = {
     "sc_linear": (_I, [_P, _P, _P, _I64, _P, _P, _P, _SZ, _P]),
     "sc_linear_ex": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _SZ, _P]),
     "sc_linear_ex_noalloc": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P]),
+    "sc_linear_allgather": (_I, [_P, _P, _P, _I64, _P, _P, _P, _I, _I, _I64, _I64, ctypes.c_uint32, _P, _SZ, _P]),
+    "sc_allgather_wait": (_I, [_P, _P, _I, ctypes.c_uint32, _P]),
+    "sc_ipc_handle": (_I, [_P, _P, _P, ctypes.POINTER(_SZ)]),
+    "sc_ipc_open": (_I, [_P, _P, _SZ, ctypes.POINTER(ctypes.c_void_p)]),
+    "sc_ipc_close": (_I, [_P, _P, _SZ]),
     "sc_linear_w8": (_I, [_P, _P, _P, _I64, _P, _P, _P, _SZ, _P]),
     "sc_linear_fp8": (_I, [_P, _P, _P, _I64, _P, _P, _P, _SZ, _P]),
     "sc_gemv_w8": (_I, [_P, _P, _P, _I64, _P, _P, _P, _SZ, _P]),

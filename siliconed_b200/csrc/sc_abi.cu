@@ -247,8 +247,8 @@ sc_status sc_ctx_create(int device, sc_ctx** out) {
     return SC_NO_DEVICE;
   }
   ctx->encode_tiled = reinterpret_cast<sc_encode_tiled_fn>(fn);
-  if (cudaMalloc(&ctx->d_err, kErrWords * sizeof(int)) != cudaSuccess ||
-      cudaMemset(ctx->d_err, 0, kErrWords * sizeof(int)) != cudaSuccess) {
+  if (cudaMalloc(&ctx->d_err, kCtxWords * sizeof(int)) != cudaSuccess ||
+      cudaMemset(ctx->d_err, 0, kCtxWords * sizeof(int)) != cudaSuccess) {
     cudaGetLastError();
     if (ctx->d_err) cudaFree(ctx->d_err);
     delete ctx;
@@ -448,6 +448,107 @@ sc_status sc_gemv_w8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
   if (m == 0) return SC_OK;
   if ((s = enter(ctx)) != SC_OK) return s;
   return run_gemv(ctx, w, x, m, bias, y, false, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+sc_status sc_linear_allgather(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
+                              void* const* y_peers, uint32_t* const* flag_peers, int world, int rank, int64_t col0,
+                              int64_t n_total, uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (w == nullptr || x == nullptr || y_peers == nullptr || flag_peers == nullptr || m < 1)
+    return fail(ctx, SC_INVALID_ARG, "null argument or m < 1");
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+    return fail(ctx, SC_INVALID_ARG, "world must be 1..8 and 0 <= rank < world");
+  if (epoch == 0) return fail(ctx, SC_INVALID_ARG, "epoch 0 is reserved (flags start at 0)");
+  if (col0 < 0 || col0 % 8 != 0 || n_total % 8 != 0 || col0 + w->n > n_total)
+    return fail(ctx, SC_UNSUPPORTED_SHAPE, "columns must be 8-aligned and inside n_total");
+  if (m > 0x7FFFFFFF || w->k > 0x7FFFFFFF || w->k % 8 != 0) return fail(ctx, SC_UNSUPPORTED_SHAPE, "bad m or K");
+  if (w->device != ctx->device) return fail(ctx, SC_INVALID_ARG, "weight registered on another device");
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) || (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 1u)))
+    return fail(ctx, SC_UNALIGNED, "x must be 16-byte aligned, bias 2-byte aligned");
+  PeerOut peers = {};
+  for (int r = 0; r < world; ++r) {
+    if (y_peers[r] == nullptr || flag_peers[r] == nullptr || (reinterpret_cast<uintptr_t>(y_peers[r]) & 15u) ||
+        (reinterpret_cast<uintptr_t>(flag_peers[r]) & 3u))
+      return fail(ctx, SC_INVALID_ARG, "every rank needs a 16-byte aligned output and a 4-byte aligned flag array");
+    peers.y[r] = y_peers[r];
+    peers.flags[r] = flag_peers[r];
+  }
+  if (workspace == nullptr || workspace_bytes < widened_bytes(w) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(ctx, SC_WORKSPACE_TOO_SMALL, "the fused gather needs a 256-byte aligned workspace of n_pad * k_pad * 2 bytes");
+  peers.world = world;
+  peers.rank = rank;
+  peers.col0 = col0;
+  peers.ld = n_total;
+  peers.epoch = epoch;
+  peers.counter = ctx->d_err + kErrWords;
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap tmx, tmw;
+  if ((s = make_tmap_x(ctx, x, m, w->k, &tmx)) != SC_OK) return s;
+  if ((s = make_tmap_widened(ctx, w, workspace, &tmw)) != SC_OK) return s;
+  if ((s = check_cuda(ctx, launch_widen(w, workspace, ctx->sm_count, st), "widen launch")) != SC_OK) return s;
+  return check_cuda(ctx, launch_gemm_bf16_peers(tmx, tmw, w, bias, peers, m, ctx->d_err, ctx->sm_count, st),
+                    "gathering gemm launch");
+}
+
+sc_status sc_allgather_wait(sc_ctx* ctx, const uint32_t* flags, int world, uint32_t epoch, void* stream) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (flags == nullptr || world < 1 || world > kMaxPeers || epoch == 0) return fail(ctx, SC_INVALID_ARG, "bad argument");
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  return check_cuda(ctx, launch_gather_wait(flags, world, epoch, ctx->d_err, static_cast<cudaStream_t>(stream)),
+                    "gather wait launch");
+}
+
+sc_status sc_ipc_handle(sc_ctx* ctx, void* device_ptr, void* handle_out, size_t* offset_out) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (device_ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+    return fail(ctx, SC_INVALID_ARG, "null argument");
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  // The handle names the whole allocation that holds device_ptr; the offset locates it inside.
+  typedef CUresult (*range_fn)(CUdeviceptr*, size_t*, CUdeviceptr);
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || fn == nullptr) {
+    cudaGetLastError();
+    return fail(ctx, SC_CUDA_ERROR, "cuMemGetAddressRange is not available");
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (reinterpret_cast<range_fn>(fn)(&base, &size, reinterpret_cast<CUdeviceptr>(device_ptr)) != CUDA_SUCCESS)
+    return fail(ctx, SC_INVALID_ARG, "not a device allocation");
+  cudaIpcMemHandle_t h;
+  if ((s = check_cuda(ctx, cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "cudaIpcGetMemHandle")) != SC_OK)
+    return s;
+  std::memcpy(handle_out, &h, sizeof h);
+  *offset_out = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(device_ptr) - base);
+  return SC_OK;
+}
+
+sc_status sc_ipc_open(sc_ctx* ctx, const void* handle, size_t offset, void** device_ptr_out) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (handle == nullptr || device_ptr_out == nullptr) return fail(ctx, SC_INVALID_ARG, "null argument");
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  void* base = nullptr;
+  if ((s = check_cuda(ctx, cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle")) !=
+      SC_OK)
+    return s;
+  *device_ptr_out = static_cast<uint8_t*>(base) + offset;
+  return SC_OK;
+}
+
+sc_status sc_ipc_close(sc_ctx* ctx, void* device_ptr, size_t offset) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (device_ptr == nullptr) return fail(ctx, SC_INVALID_ARG, "null argument");
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  return check_cuda(ctx, cudaIpcCloseMemHandle(static_cast<uint8_t*>(device_ptr) - offset), "cudaIpcCloseMemHandle");
 }
 
 sc_status sc_sync(sc_ctx* ctx, void* stream) {

@@ -43,6 +43,7 @@ struct __align__(1024) Smem {
   uint8_t a[kStages][kABytes];  // x tiles
   uint8_t b[kStages][kBBytes];  // widened weight half-tiles
   float sb[kEpiWarps][2][BN];   // per epilogue warp: the tile's scales and biases
+  uint4 stage[kEpiWarps][32 * 8];  // kPeers: per epilogue warp, 32 rows x 64 bf16 (16-byte units, swizzled)
   uint64_t full[kStages];       // leader: both CTAs' operands of the stage landed
   uint64_t empty[kStages];      // the pair's MMAs of the stage completed (leader's commit)
   uint64_t acc_full[2];
@@ -54,11 +55,16 @@ struct __align__(1024) Smem {
 
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 
-template <bool kF32Out>
+// kPeers: the fused column-parallel gather.  Each bf16 output tile goes to the output of every rank
+// (peers.y[r], rows of peers.ld elements, columns peers.col0 + j) with plain stores over NVLink; after
+// its last tile every CTA fences at system scope and counts itself on peers.counter, and the last CTA
+// raises peers.flags[r][peers.rank] = peers.epoch on every rank r (release, system scope).
+template <bool kF32Out, bool kPeers>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const float* __restrict__ scales, const uint16_t* __restrict__ bias, void* __restrict__ y_out,
-                   int M, int N, int k_tiles, int m_tiles, int n_tiles, int* err) {
+                   int M, int N, int k_tiles, int m_tiles, int n_tiles, int* err,
+                   const __grid_constant__ PeerOut peers) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -219,7 +225,35 @@ __global__ void __launch_bounds__(kThreads, 1)
             const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
             packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
           }
-          if (row < M) {
+          if (kPeers) {
+            // Two chunks (64 columns) of the warp's 32 rows gather in shared memory (16-byte units,
+            // XOR-swizzled by row), then go out to every rank's output (its own included) as 128-byte
+            // row segments: 8 lanes per row, 4 rows per store instruction, which NVLink carries far
+            // better than one 16-byte piece per row.  Columns stay 16-byte aligned (col0, ld and the
+            // shard's width are multiples of 8, checked by the host).
+            uint4* st = s.stage[ew];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              st[lane * 8 + (((ch & 1) * 4 + q) ^ (lane & 7))] =
+                  make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+            if (ch & 1) {
+              __syncwarp();
+              const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM + ew * 32;
+              const int c0 = n0 + (ch - 1) * 32;
+#pragma unroll
+              for (int it = 0; it < 8; ++it) {
+                const int u = it * 32 + lane, rr = u >> 3, cu = u & 7;
+                const int grow = row0 + rr, col = c0 + cu * 8;
+                if (grow < M && col + 8 <= N) {
+                  const uint4 v = st[rr * 8 + (cu ^ (rr & 7))];
+                  for (int r = 0; r < peers.world; ++r)
+                    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(peers.y[r]) + static_cast<int64_t>(grow) * peers.ld +
+                                              peers.col0 + col) = v;
+                }
+              }
+              __syncwarp();
+            }
+          } else if (row < M) {
             uint16_t* dst = static_cast<uint16_t*>(y_out) + static_cast<int64_t>(row) * N + n;
             if (vec_ok && n + 32 <= N) {
               uint4* d4 = reinterpret_cast<uint4*>(dst);
@@ -239,6 +273,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive_cluster(peer_addr(&s.acc_empty[acc], 0));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
+    }
+    if (kPeers) {
+      // The CTA's stores to every rank are done (all four epilogue warps meet here, on every path),
+      // then one thread fences them at system scope and counts the CTA; the last CTA signals.
+      named_barrier_sync(1, kEpiWarps * 32);
+      if (ew == 0 && lane == 0) {
+        __threadfence_system();
+        const int old = atomicAdd(peers.counter, 1);
+        if (old == static_cast<int>(gridDim.x) - 1) {
+          atomicExch(peers.counter, 0);
+          __threadfence_system();
+          for (int r = 0; r < peers.world; ++r) st_release_sys(peers.flags[r] + peers.rank, peers.epoch);
+        }
+      }
     }
   }
 
@@ -280,10 +328,10 @@ __global__ void __launch_bounds__(256) widen_codes(const uint4* __restrict__ cod
   }
 }
 
-template <bool kF32Out>
+template <bool kF32Out, bool kPeers>
 cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const sc_weight* w, const uint16_t* bias,
-                        void* y, int64_t m, int* err, int sm_count, cudaStream_t stream) {
-  auto kernel = gemm_bf16_pair<kF32Out>;
+                        void* y, int64_t m, int* err, int sm_count, cudaStream_t stream, const PeerOut& peers) {
+  auto kernel = gemm_bf16_pair<kF32Out, kPeers>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e =
@@ -310,7 +358,21 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias, y,
-                            static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err);
+                            static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers);
+}
+
+// One rank waits until every rank's flag for it reached `epoch` (epochs only grow), bounded.
+__global__ void gather_wait(const uint32_t* __restrict__ flags, int world, uint32_t epoch, int* err) {
+  if (threadIdx.x != 0) return;
+  const unsigned long long t0 = global_ns();
+  for (int r = 0; r < world; ++r) {
+    while (static_cast<int32_t>(ld_acquire_sys(flags + r) - epoch) < 0) {
+      if (global_ns() - t0 > kWaitLimitNs) {
+        record_error(err, kErrTimeout, kSiteGather);
+        return;
+      }
+    }
+  }
 }
 
 }  // namespace gemm_bf16
@@ -335,8 +397,20 @@ cudaError_t launch_widen(const sc_weight* w, void* out, int sm_count, cudaStream
 cudaError_t launch_gemm_bf16(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
                              const uint16_t* bias, void* y, bool f32_out, int64_t m, int* err, int sm_count,
                              cudaStream_t stream) {
-  return f32_out ? gemm_bf16::launch_gemm<true>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream)
-                 : gemm_bf16::launch_gemm<false>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream);
+  const PeerOut none = {};
+  return f32_out ? gemm_bf16::launch_gemm<true, false>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream, none)
+                 : gemm_bf16::launch_gemm<false, false>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream, none);
+}
+
+cudaError_t launch_gemm_bf16_peers(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
+                                   const uint16_t* bias, const PeerOut& peers, int64_t m, int* err, int sm_count,
+                                   cudaStream_t stream) {
+  return gemm_bf16::launch_gemm<false, true>(tmap_x, tmap_w, w, bias, nullptr, m, err, sm_count, stream, peers);
+}
+
+cudaError_t launch_gather_wait(const uint32_t* flags, int world, uint32_t epoch, int* err, cudaStream_t stream) {
+  gemm_bf16::gather_wait<<<1, 32, 0, stream>>>(flags, world, epoch, err);
+  return cudaGetLastError();
 }
 
 }  // namespace sc

@@ -15,6 +15,7 @@ namespace sc {
 constexpr int kArenaKAlign = 64;    // the GEMM's BK (one 128-byte swizzle row of bf16)
 constexpr int kArenaNAlign = 256;   // the GEMM's BN
 constexpr int kErrWords = 4;        // device error word: code, site, block, spare
+constexpr int kCtxWords = 8;        // the context's device ints: the error word, then the gather counter
 
 // Codes of the padding: q = 0 in the stored encoding of each kind.
 constexpr uint8_t kPadInt8 = 0x80;  // int8 is stored biased, u = q + 128
@@ -28,7 +29,8 @@ typedef CUresult (*sc_encode_tiled_fn)(CUtensorMap*, CUtensorMapDataType, cuuint
 struct sc_ctx {
   int device = -1;
   int sm_count = 0;
-  int* d_err = nullptr;  // sc::kErrWords ints on the device
+  int* d_err = nullptr;  // sc::kCtxWords ints on the device: the error word (kErrWords), then the
+                         // fused gather's CTA counter (zero between launches)
   sc_encode_tiled_fn encode_tiled = nullptr;
   std::string last_error;
 };
@@ -77,6 +79,24 @@ cudaError_t launch_widen(const sc_weight* w, void* out, int sm_count, cudaStream
 cudaError_t launch_gemm_bf16(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
                              const uint16_t* bias, void* y, bool f32_out, int64_t m, int* err, int sm_count,
                              cudaStream_t stream);
+
+// The fused column-parallel gather (multi-GPU): the bf16-operand pair GEMM whose epilogue stores every
+// output tile into the output of each of `world` ranks (peer pointers over NVLink), at columns col0 +
+// j of rows of `ld` elements; its last CTA raises flags[r][rank] = epoch on every rank r.  And the
+// bounded wait of one rank for the flags of all ranks.
+constexpr int kMaxPeers = 8;
+struct PeerOut {
+  void* y[kMaxPeers];
+  uint32_t* flags[kMaxPeers];
+  int world, rank;
+  int64_t col0, ld;
+  uint32_t epoch;
+  int* counter;
+};
+cudaError_t launch_gemm_bf16_peers(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
+                                   const uint16_t* bias, const PeerOut& peers, int64_t m, int* err, int sm_count,
+                                   cudaStream_t stream);
+cudaError_t launch_gather_wait(const uint32_t* flags, int world, uint32_t epoch, int* err, cudaStream_t stream);
 
 // CTA count and workspace of the skinny product.
 int gemv_splits(const sc_weight* w, int64_t m, int sm_count);

@@ -25,6 +25,7 @@ enum WaitSite : int {
   kSiteMmaAccum = 6,
   kSiteEpilogueFull = 7,
   kSiteDrain = 8,
+  kSiteGather = 9,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -103,6 +104,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       }
     }
   }
+}
+
+// Flags between GPUs (the fused gather): system-scope acquire load and release store.
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // mbar_wait by polling with the non-suspending probe.

@@ -101,3 +101,91 @@ def quantized_column_parallel(ctx, codes, kind: int, scales, n: int, *, publishe
         return local
 
     return ColumnParallelLinear(n, make_local, group=group)
+
+
+class FusedColumnParallelLinear:
+    """The column-parallel linear with the all-gather fused into the product (``sc_linear_allgather``).
+
+    Rank r registers its columns [n0, n1) and, every call, multiplies the whole x by them; the product's
+    epilogue stores each output tile into every rank's y over NVLink (peer pointers opened once with
+    CUDA IPC) and raises an epoch flag on every rank; ``sc_allgather_wait`` holds the stream until all
+    ranks' columns have landed.  y is double-buffered (a rank may start call e + 1 while another still
+    reads call e's result): the returned tensor stays valid until the call after next.  Set-up is
+    collective (every rank of ``group`` constructs it); so is every call, with the same x shape.
+    """
+
+    def __init__(self, ctx, codes, kind: int, scales, n: int, m_max: int, *, published_nk: bool = False,
+                 bias=None, group=None, stream=None):
+        import ctypes
+        from . import abi
+        from .products import QuantizedWeight
+        self.ctx, self.group = ctx, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks")
+        self.n = n
+        self.ranges = column_ranges(n, self.world, 8)
+        self.n0, self.n1 = self.ranges[self.rank]
+        if self.n1 <= self.n0:
+            raise ValueError("every rank needs columns")
+        self.w = QuantizedWeight(ctx, codes, kind, scales, published_nk=published_nk, columns=(self.n0, self.n1),
+                                 stream=stream)
+        self.bias = None if bias is None else bias[self.n0:self.n1].contiguous()
+        dev = torch.device("cuda", ctx.device)
+        self.m_max = m_max
+        self.y = [torch.empty((m_max, n), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        self.flags = torch.zeros(self.world, dtype=torch.int32, device=dev)
+        self.ws = torch.empty(max(self.w.workspace_bytes(max(m_max, 1536)), 256), dtype=torch.uint8, device=dev)
+        lib = ctx.lib
+        mine = []
+        for t in (self.y[0], self.y[1], self.flags):
+            h = (ctypes.c_uint8 * 64)()
+            off = ctypes.c_size_t()
+            ctx.check(lib.sc_ipc_handle(ctx.ptr, ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off)))
+            mine.append((bytes(h), int(off.value)))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        self._opened = []  # (pointer, offset) to close
+        self.peer_y = [[0] * self.world for _ in range(2)]
+        self.peer_flags = [0] * self.world
+        for r, handles in enumerate(everyone):
+            ptrs = []
+            for (h, off), t in zip(handles, (self.y[0], self.y[1], self.flags)):
+                if r == self.rank:
+                    ptrs.append(t.data_ptr())
+                    continue
+                p = ctypes.c_void_p()
+                buf = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+                ctx.check(lib.sc_ipc_open(ctx.ptr, buf, off, ctypes.byref(p)))
+                self._opened.append((p.value, off))
+                ptrs.append(p.value)
+            self.peer_y[0][r], self.peer_y[1][r], self.peer_flags[r] = ptrs
+        self._y_arr = [(ctypes.c_void_p * self.world)(*self.peer_y[i]) for i in range(2)]
+        self._f_arr = (ctypes.c_void_p * self.world)(*self.peer_flags)
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def __call__(self, x: torch.Tensor, stream=None) -> torch.Tensor:
+        import ctypes
+        m = x.shape[0]
+        if m > self.m_max or x.shape[1] != self.w.k:
+            raise ValueError(f"x must be [<= {self.m_max}, {self.w.k}]")
+        self.epoch += 1
+        buf = self.epoch % 2
+        lib, ctx = self.ctx.lib, self.ctx
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream if stream is None else stream.cuda_stream)
+        b = None if self.bias is None else ctypes.c_void_p(self.bias.data_ptr())
+        ctx.check(lib.sc_linear_allgather(ctx.ptr, self.w.ptr, ctypes.c_void_p(x.data_ptr()), m, b, self._y_arr[buf],
+                                          self._f_arr, self.world, self.rank, self.n0, self.n, self.epoch,
+                                          ctypes.c_void_p(self.ws.data_ptr()), self.ws.numel(), st))
+        ctx.check(lib.sc_allgather_wait(ctx.ptr, ctypes.c_void_p(self.flags.data_ptr()), self.world, self.epoch, st))
+        return self.y[buf][:m]
+
+    def close(self) -> None:
+        import ctypes
+        torch.cuda.synchronize()
+        for p, off in self._opened:
+            self.ctx.lib.sc_ipc_close(self.ctx.ptr, ctypes.c_void_p(p), off)
+        self._opened = []
+        self.w.close()
