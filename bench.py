@@ -128,11 +128,13 @@ class ClockSampler:
 
 def route_kernels(case, ws_bytes: int) -> list[str]:
     """The library's kernels one product of this case launches (the step the roofline's `achieved`
-    covers): the GEMV for m <= 32 (one launch per pass of up to 8 rows), the single-CTA GEMM up to
-    128 rows, the fused pair kernel above, and from 1536 rows with a workspace the widening of the
+    covers): the GEMV up to 4 rows, the skinny tensor-core product up to 32, the single-CTA GEMM up
+    to 128 rows, the fused pair kernel above, and from 1536 rows with a workspace the widening of the
     codes followed by the bf16-operand pair GEMM."""
+    if case.m <= 4:
+        return ["gemv_w8"]
     if case.m <= 32:
-        return ["gemv_w8"] * (-(-case.m // 8))
+        return ["gemm_w8_skinny"]
     if case.m <= 128:
         return ["gemm_w8_tc"]
     if ws_bytes > 0:

@@ -89,10 +89,10 @@ sc_status enter(sc_ctx* ctx) {
   return SC_OK;
 }
 
-sc_status make_tmap_x(sc_ctx* ctx, const sc_bf16* x, int64_t m, int64_t k, CUtensorMap* map) {
+sc_status make_tmap_x(sc_ctx* ctx, const sc_bf16* x, int64_t m, int64_t k, CUtensorMap* map, int box_rows = 128) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
-  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<sc_bf16*>(x), dims, strides, box,
                                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -170,8 +170,13 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
   if (m == 0) return SC_OK;
   if ((s = enter(ctx)) != SC_OK) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (m <= 32) return run_gemv(ctx, w, x, m, bias, y, f32_out, workspace, workspace_bytes, st);
+  if (m <= kSkinnyMinRows) return run_gemv(ctx, w, x, m, bias, y, f32_out, workspace, workspace_bytes, st);
   CUtensorMap tmx;
+  if (m <= 32) {
+    if ((s = make_tmap_x(ctx, x, m, w->k, &tmx, gemm_skinny_box_rows(m))) != SC_OK) return s;
+    return check_cuda(ctx, launch_gemm_skinny(tmx, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
+                      "skinny gemm launch");
+  }
   if ((s = make_tmap_x(ctx, x, m, w->k, &tmx)) != SC_OK) return s;
   if (m > kPairMinRows) {
     // With a workspace for the widened weight: widen once, then the bf16-operand pair GEMM (the

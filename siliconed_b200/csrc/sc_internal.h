@@ -98,6 +98,13 @@ cudaError_t launch_gemm_bf16_peers(const CUtensorMap& tmap_x, const CUtensorMap&
                                    cudaStream_t stream);
 cudaError_t launch_gather_wait(const uint32_t* flags, int world, uint32_t epoch, int* err, cudaStream_t stream);
 
+// The skinny product on the tensor cores (4 < m <= 32): the x tensor map's box rows for m, and the launch.
+int gemm_skinny_box_rows(int64_t m);
+cudaError_t launch_gemm_skinny(const CUtensorMap& tmap_x, const sc_weight* w, const uint16_t* bias, void* y,
+                               bool f32_out, int64_t m, int* err, int sm_count, cudaStream_t stream);
+// Rows above which sc_linear leaves the GEMV for the skinny tensor-core product.
+constexpr int64_t kSkinnyMinRows = 4;
+
 // CTA count and workspace of the skinny product.
 int gemv_splits(const sc_weight* w, int64_t m, int sm_count);
 size_t gemv_workspace_bytes(const sc_weight* w, int64_t m, int sm_count);

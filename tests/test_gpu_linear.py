@@ -221,6 +221,37 @@ def test_gemv_e4m3_matches_oracle(ctx, m):
     check_against_oracle(ctx, abi.WEIGHT_E4M3, x, q, s, None, f"gemv e4m3 m={m}")
 
 
+@pytest.mark.parametrize("kind,m,nan", [(abi.WEIGHT_INT8, 5, False), (abi.WEIGHT_INT8, 9, False), (abi.WEIGHT_INT8, 16, False),
+                                         (abi.WEIGHT_INT8, 24, False), (abi.WEIGHT_E4M3, 32, True)])
+def test_skinny_tensor_core_product_agrees_with_gemv(ctx, kind, m, nan):
+    """4 < m <= 32 runs on the tensor cores (K split over a cluster, partial sums added in rank order
+    through distributed shared memory); sc_gemv_w8 forces the CUDA-core GEMV on the same inputs."""
+    k, n = 4096, 1000
+    g = np.random.default_rng(300 + m)
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    if kind == abi.WEIGHT_INT8:
+        q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+    else:
+        q = configs.to_e4m3_codes(g.standard_normal((k, n), dtype=np.float32) * 4)
+        q[(q & 0x7F) == 0x7F] ^= 1
+        if nan:
+            q[g.integers(0, k, 5), g.integers(0, n, 5)] = 0x7F
+    s = (np.abs(g.standard_normal(n)) * 0.004 / 127 + 1e-7).astype(np.float32)
+    b = configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.01)
+    w = QuantizedWeight(ctx, q, kind, s)
+    xd, bd = bf16_dev(x), bf16_dev(b)
+    tc = f32_of_bf16(bf16_host(w.linear(xd, bias=bd)))
+    gv = f32_of_bf16(bf16_host(w.gemv(xd, bias=bd)))
+    ctx.poll_errors()
+    assert np.array_equal(np.isnan(tc), np.isnan(gv))
+    keep = ~np.isnan(gv)
+    assert nan or keep.all()
+    e = rel_l2(tc[keep], gv[keep])
+    mx = float(np.max(np.abs(tc[keep].astype(np.float64) - gv[keep])))
+    assert e <= REL_L2_BF16 and mx <= MAX_ABS_BF16, (e, mx)
+    w.close()
+
+
 def test_gemv_meets_the_reference_bar(ctx):
     """Qwen3VLDecoderTests.swift:250-263 on its own inputs (x rounded to bf16): per-channel relative
     L2 against fp64, median < 1e-6 and worst < 5e-6, for every scale type."""
