@@ -151,6 +151,24 @@ SC_API sc_status sc_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, in
 SC_API sc_status sc_linear_ex(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, void* y,
                               sc_out_type y_type, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Operation fused into the epilogue of sc_linear_epilogue, applied to v = acc * s[n] + bias[n] (fp32). */
+typedef enum sc_epilogue {
+    SC_EPI_GELU_TANH = 1,       /* y bf16 [m, n] = bf16(gelu_tanh(v)): one rounding instead of two */
+    SC_EPI_GATED_RESIDUAL = 2   /* y fp32 [m, n] (read and written) = fmaf(gate[n], v, y) */
+} sc_epilogue;
+
+/* The bf16-operand product of the widened route (see sc_workspace_size) with an elementwise stage of
+ * the DiT block fused into its epilogue, so that the product's output never goes through HBM as an
+ * intermediate.  No counterpart in the reference, which runs the GELU (AnimaGELU,
+ * ElementwiseGPU.swift) and the gated residual (x + gate * y, DiT.swift) as passes of their own.
+ * gate: fp32 [n], device memory, used by SC_EPI_GATED_RESIDUAL only (NULL otherwise).  Takes m > 128
+ * rows and a 256-byte aligned workspace of at least n_pad * k_pad * 2 bytes (N rounded up to 256, K
+ * to 64), whatever m is; otherwise SC_UNSUPPORTED_SHAPE or SC_WORKSPACE_TOO_SMALL.  y must not
+ * overlap x. */
+SC_API sc_status sc_linear_epilogue(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
+                                    void* y, sc_epilogue op, const float* gate, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
 /* sc_linear_ex with its scratch in a 32 MiB device array of the library instead of a workspace: it
  * allocates nothing and takes no workspace argument.  No counterpart in the reference: it serves
  * callers that have no scratch buffer to pass (a binding that keeps the signature of

@@ -26,6 +26,7 @@ SCALE_F32, SCALE_BF16, SCALE_F16 = 1, 2, 3
 SCALE_TENSOR, SCALE_COLUMNS = 0, 1
 VALUES_ON_DEVICE, PUBLISHED_NK = 0x1, 0x2
 OUT_BF16, OUT_F32 = 0, 1
+EPI_GELU_TANH, EPI_GATED_RESIDUAL = 1, 2
 
 _P, _I64, _I, _U32, _SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint32, ctypes.c_size_t
 _PP = ctypes.POINTER(ctypes.c_void_p)
@@ -45,6 +46,7 @@ SIGNATURES = {
     "sc_workspace_size": (_I, [_P, _P, _I64, ctypes.POINTER(_SZ)]),
     "sc_linear": (_I, [_P, _P, _P, _I64, _P, _P, _P, _SZ, _P]),
     "sc_linear_ex": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _SZ, _P]),
+    "sc_linear_epilogue": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _P, _SZ, _P]),
     "sc_linear_ex_noalloc": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P]),
     "sc_linear_allgather": (_I, [_P, _P, _P, _I64, _P, _P, _P, _I, _I, _I64, _I64, ctypes.c_uint32, _P, _SZ, _P]),
     "sc_allgather_wait": (_I, [_P, _P, _I, ctypes.c_uint32, _P]),

@@ -141,10 +141,10 @@ __global__ void __launch_bounds__(kRowThreads) gated_residual_k(float* __restric
       o = make_float4(o.x * inv * w.x, o.y * inv * w.y, o.z * inv * w.z, o.w * inv * w.w);
     }
     float4 a = xr[i];
-    a.x = a.x + g.x * o.x;
-    a.y = a.y + g.y * o.y;
-    a.z = a.z + g.z * o.z;
-    a.w = a.w + g.w * o.w;
+    a.x = fmaf(g.x, o.x, a.x);
+    a.y = fmaf(g.y, o.y, a.y);
+    a.z = fmaf(g.z, o.z, a.z);
+    a.w = fmaf(g.w, o.w, a.w);
     xr[i] = a;
   }
 }

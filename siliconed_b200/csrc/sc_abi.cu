@@ -435,6 +435,30 @@ sc_status sc_linear_ex(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_
   return run_linear(ctx, w, x, m, bias, y, y_type == SC_OUT_F32, workspace, workspace_bytes, stream, 0);
 }
 
+sc_status sc_linear_epilogue(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
+                             void* y, sc_epilogue op, const float* gate, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  sc_status s = check_product_args(ctx, w, x, m, bias, y);
+  if (s != SC_OK) return s;
+  if (op != SC_EPI_GELU_TANH && op != SC_EPI_GATED_RESIDUAL) return fail(ctx, SC_INVALID_ARG, "unknown epilogue");
+  if (op == SC_EPI_GATED_RESIDUAL && (gate == nullptr || !is_device_pointer(gate) ||
+                                      (reinterpret_cast<uintptr_t>(gate) & 3u)))
+    return fail(ctx, SC_INVALID_ARG, "the gated residual needs a 4-byte aligned device gate of n floats");
+  if (m == 0) return SC_OK;
+  if (m <= kPairMinRows) return fail(ctx, SC_UNSUPPORTED_SHAPE, "sc_linear_epilogue takes more than 128 rows");
+  if (workspace == nullptr || workspace_bytes < widened_bytes(w) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(ctx, SC_WORKSPACE_TOO_SMALL, "sc_linear_epilogue needs a 256-byte aligned workspace of n_pad * k_pad * 2 bytes");
+  if ((s = enter(ctx)) != SC_OK) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap tmx, tmw;
+  if ((s = make_tmap_x(ctx, x, m, w->k, &tmx)) != SC_OK) return s;
+  if ((s = make_tmap_widened(ctx, w, workspace, &tmw)) != SC_OK) return s;
+  if ((s = check_cuda(ctx, launch_widen(w, workspace, ctx->sm_count, st), "widen launch")) != SC_OK) return s;
+  return check_cuda(ctx, launch_gemm_bf16_op(tmx, tmw, w, bias, y, static_cast<int>(op), gate, m, ctx->d_err,
+                                             ctx->sm_count, st),
+                    "epilogue gemm launch");
+}
+
 sc_status sc_linear_w8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,
                        void* workspace, size_t workspace_bytes, void* stream) {
   return run_linear(ctx, w, x, m, bias, y, false, workspace, workspace_bytes, stream, SC_WEIGHT_INT8);

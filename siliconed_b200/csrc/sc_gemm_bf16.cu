@@ -43,6 +43,7 @@ struct __align__(1024) Smem {
   uint8_t a[kStages][kABytes];  // x tiles
   uint8_t b[kStages][kBBytes];  // widened weight half-tiles
   float sb[kEpiWarps][2][BN];   // per epilogue warp: the tile's scales and biases
+  float sb2[kEpiWarps][BN];      // kOpResidual: per epilogue warp, the tile's gates
   uint4 stage[kEpiWarps][32 * 8];  // kPeers: per epilogue warp, 32 rows x 64 bf16 (16-byte units, swizzled)
   uint64_t full[kStages];       // leader: both CTAs' operands of the stage landed
   uint64_t empty[kStages];      // the pair's MMAs of the stage completed (leader's commit)
@@ -59,12 +60,28 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 // (peers.y[r], rows of peers.ld elements, columns peers.col0 + j) with plain stores over NVLink; after
 // its last tile every CTA fences at system scope and counts itself on peers.counter, and the last CTA
 // raises peers.flags[r][peers.rank] = peers.epoch on every rank r (release, system scope).
-template <bool kF32Out, bool kPeers>
+//
+// kOp: the epilogue's operation after v = acc * scale + bias (fp32).  kOpNone stores v; kOpGelu stores
+// bf16(gelu_tanh(v)) (one rounding, where a separate pass would round v first); kOpResidual adds
+// gate[n] * v to the fp32 output in place, x = fma(gate, v, x) (the gated residual stream).
+constexpr int kOpNone = 0, kOpGelu = 1, kOpResidual = 2;
+
+// gelu_tanh(v) = 0.5 v (1 + tanh(u)), u = sqrt(2 / pi) (v + 0.044715 v^3), through the identity
+// 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)): one exponential and one approximate division, about 2e-6
+// relative error before the bf16 rounding.  exp overflows to +inf for v below about -11: v / inf = -0.
+__device__ __forceinline__ float gelu_tanh(float v) {
+  const float e = __expf(-1.5957691216057308f * fmaf(0.044715f * v, v * v, v));
+  return __fdividef(v, 1.0f + e);
+}
+
+template <bool kF32Out, bool kPeers, int kOp>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const float* __restrict__ scales, const uint16_t* __restrict__ bias, void* __restrict__ y_out,
                    int M, int N, int k_tiles, int m_tiles, int n_tiles, int* err,
-                   const __grid_constant__ PeerOut peers) {
+                   const __grid_constant__ PeerOut peers, const float* __restrict__ gate) {
+  static_assert(kOp != kOpResidual || kF32Out, "the residual is fp32");
+  static_assert(kOp != kOpGelu || !kF32Out, "the GELU output is bf16");
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -105,7 +122,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0, issued = 0, last_parity = 0;
       for (int tile = pair; tile < num_tiles && !*abort; tile += pairs) {
-        const int mt = tile % m_tiles, nt = tile / m_tiles;
+        int mt, nt;
+        tile_coords(tile, m_tiles, n_tiles, mt, nt);
         const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM;
         const int col0 = nt * BN + static_cast<int>(rank) * BNH;
         for (int kt = 0; kt < k_tiles; ++kt) {
@@ -176,7 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     const bool vec_ok = (N % 8) == 0, vec4_ok = (N % 4) == 0;
     for (int tile = pair; tile < num_tiles; tile += pairs) {
-      const int mt = tile % m_tiles, nt = tile / m_tiles;
+      int mt, nt;
+      tile_coords(tile, m_tiles, n_tiles, mt, nt);
       const int n0 = nt * BN;
       const int row = mt * 2 * BM + static_cast<int>(rank) * BM + ew * 32 + lane;
       __syncwarp();
@@ -184,8 +203,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n = n0 + c;
         s_scale[c] = scales[n];
         s_bias[c] = (bias != nullptr && n < N) ? __uint_as_float(static_cast<uint32_t>(bias[n]) << 16) : 0.0f;
+        if (kOp == kOpResidual) s.sb2[ew][c] = n < N ? gate[n] : 0.0f;
       }
       __syncwarp();
+      // Stores leave through the warp's staging buffer: each lane holds one row of a 32-column chunk
+      // (its TMEM lane), the chunk is written to shared memory (16-byte units, XOR-swizzled by row)
+      // and read back so that 8 lanes cover 128 contiguous bytes of one row: 4 rows per store
+      // instruction instead of 32, which the L2 and the memory controllers take far better.
+      // kOpResidual reads the residual tile the same way, one chunk ahead of its use (the first
+      // chunk before the accumulator is ready): one load round trip per tile is exposed, not one
+      // per chunk.  The staged paths need 16-byte aligned rows (N % 8 == 0 for bf16, N % 4 == 0 for
+      // fp32); other shapes store one row per lane.
+      const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM + ew * 32;
+      uint4* st = s.stage[ew];
+      float* xres = kOp == kOpResidual ? static_cast<float*>(y_out) : nullptr;
+      const bool res_fast = kOp == kOpResidual && vec4_ok && n0 + BN <= N;
+      float4 xcur[8];
+      if (kOp == kOpResidual && res_fast) {
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int grow = row0 + ((it * 32 + lane) >> 3);
+          xcur[it] = grow < M ? ld_cg_f4(xres + static_cast<int64_t>(grow) * N + n0 + (lane & 7) * 4)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
       int ready = 0;
       if (lane == 0) ready = mbar_wait(&s.acc_full[acc], acc_phase, abort, err, kSiteEpilogueFull) ? 1 : 0;
       if (!__shfl_sync(0xFFFFFFFFu, ready, 0)) break;
@@ -193,6 +234,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tbase = tmem + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
       for (int ch = 0; ch < BN / 32; ++ch) {
+        float4 xnext[8];
+        if (kOp == kOpResidual && res_fast && ch + 1 < BN / 32) {
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int grow = row0 + ((it * 32 + lane) >> 3);
+            xnext[it] = grow < M ? ld_cg_f4(xres + static_cast<int64_t>(grow) * N + n0 + (ch + 1) * 32 + (lane & 7) * 4)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
         uint32_t r[32];
         tmem_ld_32(tbase + ch * 32, r);
         tmem_wait_ld();
@@ -202,14 +252,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j)
             r[j] = __float_as_uint(
                 __fadd_rn(__fmul_rn(__uint_as_float(r[j]), s_scale[ch * 32 + j]), s_bias[ch * 32 + j]));
-          if (row < M) {
+          const bool staged = kOp == kOpResidual ? res_fast : vec4_ok;
+          if (staged) {
+            // 32 rows x 32 fp32: row `lane`'s 16-byte unit q at st[lane * 8 + (q ^ (lane & 7))]
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              st[lane * 8 + (q ^ (lane & 7))] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+            __syncwarp();
+            const int cu = lane & 7, col = n + cu * 4;
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+              const int rr = (it * 32 + lane) >> 3, grow = row0 + rr;
+              const uint4 u = st[rr * 8 + (cu ^ (rr & 7))];
+              float* dst = static_cast<float*>(y_out) + static_cast<int64_t>(grow) * N + col;
+              if (kOp == kOpResidual) {
+                // x = fmaf(gate, v, x): the fp32 residual stream, in place (the tile lies inside N)
+                if (grow < M) {
+                  const float* g = s.sb2[ew] + ch * 32 + cu * 4;
+                  const float4 xv = xcur[it];
+                  *reinterpret_cast<float4*>(dst) =
+                      make_float4(__fmaf_rn(g[0], __uint_as_float(u.x), xv.x), __fmaf_rn(g[1], __uint_as_float(u.y), xv.y),
+                                  __fmaf_rn(g[2], __uint_as_float(u.z), xv.z), __fmaf_rn(g[3], __uint_as_float(u.w), xv.w));
+                }
+              } else if (grow < M) {
+                if (col + 4 <= N) {
+                  *reinterpret_cast<uint4*>(dst) = u;
+                } else {
+                  for (int k = 0; col + k < N; ++k)
+                    dst[k] = __uint_as_float(k == 0 ? u.x : k == 1 ? u.y : u.z);
+                }
+              }
+            }
+            __syncwarp();
+            if (kOp == kOpResidual) {
+#pragma unroll
+              for (int it = 0; it < 8; ++it) xcur[it] = xnext[it];
+            }
+          } else if (row < M) {
             float* dst = static_cast<float*>(y_out) + static_cast<int64_t>(row) * N + n;
-            if (vec4_ok && n + 32 <= N) {
-              uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) d4[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+            if (kOp == kOpResidual) {
+              const float* g = s.sb2[ew] + ch * 32;
+              for (int j = 0; j < 32; ++j)
+                if (n + j < N) dst[j] = __fmaf_rn(g[j], __uint_as_float(r[j]), dst[j]);
             } else {
-#pragma unroll
               for (int j = 0; j < 32; ++j)
                 if (n + j < N) dst[j] = __uint_as_float(r[j]);
             }
@@ -218,53 +303,59 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            const float v0 =
-                __fadd_rn(__fmul_rn(__uint_as_float(r[j]), s_scale[ch * 32 + j]), s_bias[ch * 32 + j]);
-            const float v1 = __fadd_rn(__fmul_rn(__uint_as_float(r[j + 1]), s_scale[ch * 32 + j + 1]),
-                                       s_bias[ch * 32 + j + 1]);
+            float v0 = __fadd_rn(__fmul_rn(__uint_as_float(r[j]), s_scale[ch * 32 + j]), s_bias[ch * 32 + j]);
+            float v1 = __fadd_rn(__fmul_rn(__uint_as_float(r[j + 1]), s_scale[ch * 32 + j + 1]),
+                                 s_bias[ch * 32 + j + 1]);
+            if (kOp == kOpGelu) {
+              v0 = gelu_tanh(v0);
+              v1 = gelu_tanh(v1);
+            }
             const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
             packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
           }
-          if (kPeers) {
-            // Two chunks (64 columns) of the warp's 32 rows gather in shared memory (16-byte units,
-            // XOR-swizzled by row), then go out to every rank's output (its own included) as 128-byte
-            // row segments: 8 lanes per row, 4 rows per store instruction, which NVLink carries far
-            // better than one 16-byte piece per row.  Columns stay 16-byte aligned (col0, ld and the
-            // shard's width are multiples of 8, checked by the host).
-            uint4* st = s.stage[ew];
+          if (kPeers || vec_ok) {
+            // Two chunks (64 columns) of the warp's 32 rows gather in the staging buffer, then go out
+            // as 128-byte row segments: to this GPU's y, or (kPeers) to every rank's output, its own
+            // included, which NVLink carries far better than one 16-byte piece per row.  Peer columns
+            // stay 16-byte aligned (col0, ld and the shard's width are multiples of 8, checked by the
+            // host).
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               st[lane * 8 + (((ch & 1) * 4 + q) ^ (lane & 7))] =
                   make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
             if (ch & 1) {
               __syncwarp();
-              const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM + ew * 32;
               const int c0 = n0 + (ch - 1) * 32;
 #pragma unroll
               for (int it = 0; it < 8; ++it) {
                 const int u = it * 32 + lane, rr = u >> 3, cu = u & 7;
                 const int grow = row0 + rr, col = c0 + cu * 8;
-                if (grow < M && col + 8 <= N) {
-                  const uint4 v = st[rr * 8 + (cu ^ (rr & 7))];
-                  for (int r = 0; r < peers.world; ++r)
-                    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(peers.y[r]) + static_cast<int64_t>(grow) * peers.ld +
-                                              peers.col0 + col) = v;
+                if (grow >= M || col >= N) continue;
+                const uint4 v = st[rr * 8 + (cu ^ (rr & 7))];
+                if (kPeers) {
+                  if (col + 8 <= N)
+                    for (int r = 0; r < peers.world; ++r)
+                      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(peers.y[r]) +
+                                                static_cast<int64_t>(grow) * peers.ld + peers.col0 + col) = v;
+                } else {
+                  uint16_t* dst = static_cast<uint16_t*>(y_out) + static_cast<int64_t>(grow) * N + col;
+                  if (col + 8 <= N) {
+                    *reinterpret_cast<uint4*>(dst) = v;
+                  } else {
+                    for (int k = 0; col + k < N; ++k) {
+                      const uint32_t word = k < 2 ? v.x : k < 4 ? v.y : k < 6 ? v.z : v.w;
+                      dst[k] = static_cast<uint16_t>(word >> (16 * (k & 1)));
+                    }
+                  }
                 }
               }
               __syncwarp();
             }
           } else if (row < M) {
             uint16_t* dst = static_cast<uint16_t*>(y_out) + static_cast<int64_t>(row) * N + n;
-            if (vec_ok && n + 32 <= N) {
-              uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
-                d4[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n + j < N) dst[j] = static_cast<uint16_t>(packed[j / 2] >> (16 * (j & 1)));
-            }
+            for (int j = 0; j < 32; ++j)
+              if (n + j < N) dst[j] = static_cast<uint16_t>(packed[j / 2] >> (16 * (j & 1)));
           }
         }
       }
@@ -300,38 +391,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Widens the arena's codes [n_pad][k_pad] to bf16 in the same layout: 16 codes per thread and step,
-// four steps in flight per thread.
+// Widens the arena's codes [n_pad][k_pad] to bf16 in the same layout.  Each thread takes kPer
+// 16-code chunks a block-width apart and issues all their loads before converting (the grid is sized
+// so that every thread has kPer chunks, which keeps enough loads in flight for HBM).
+constexpr int kWidenPer = 4;
+
 template <int kKind, bool kNaN>
 __global__ void __launch_bounds__(256) widen_codes(const uint4* __restrict__ codes, uint4* __restrict__ out,
                                                     int64_t chunks) {
-  constexpr int kUnroll = 4;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  for (; i + (kUnroll - 1) * stride < chunks; i += kUnroll * stride) {
-    uint4 in[kUnroll];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * (256 * kWidenPer) + threadIdx.x;
+  uint4 in[kWidenPer];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) in[u] = __ldcs(codes + i + u * stride);
+  for (int u = 0; u < kWidenPer; ++u) {
+    const int64_t i = base + u * 256;
+    in[u] = i < chunks ? __ldcs(codes + i) : make_uint4(0, 0, 0, 0);
+  }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+  for (int u = 0; u < kWidenPer; ++u) {
+    const int64_t i = base + u * 256;
+    if (i < chunks) {
       uint4 lo, hi;
       codes16_to_bf16<kKind, kNaN>(in[u], lo, hi);
-      out[2 * (i + u * stride)] = lo;
-      out[2 * (i + u * stride) + 1] = hi;
+      out[2 * i] = lo;
+      out[2 * i + 1] = hi;
     }
-  }
-  for (; i < chunks; i += stride) {
-    uint4 lo, hi;
-    codes16_to_bf16<kKind, kNaN>(__ldcs(codes + i), lo, hi);
-    out[2 * i] = lo;
-    out[2 * i + 1] = hi;
   }
 }
 
-template <bool kF32Out, bool kPeers>
+template <bool kF32Out, bool kPeers, int kOp = kOpNone>
 cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const sc_weight* w, const uint16_t* bias,
-                        void* y, int64_t m, int* err, int sm_count, cudaStream_t stream, const PeerOut& peers) {
-  auto kernel = gemm_bf16_pair<kF32Out, kPeers>;
+                        void* y, int64_t m, int* err, int sm_count, cudaStream_t stream, const PeerOut& peers,
+                        const float* gate = nullptr) {
+  auto kernel = gemm_bf16_pair<kF32Out, kPeers, kOp>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e =
@@ -358,7 +449,7 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias, y,
-                            static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers);
+                            static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers, gate);
 }
 
 // One rank waits until every rank's flag for it reached `epoch` (epochs only grow), bounded.
@@ -380,9 +471,12 @@ __global__ void gather_wait(const uint32_t* __restrict__ flags, int world, uint3
 size_t widened_bytes(const sc_weight* w) { return static_cast<size_t>(w->n_pad) * static_cast<size_t>(w->k_pad) * 2; }
 
 cudaError_t launch_widen(const sc_weight* w, void* out, int sm_count, cudaStream_t stream) {
+  (void)sm_count;
   const int64_t chunks = w->n_pad * w->k_pad / 16;
-  const int64_t want = (chunks + 255) / 256;
-  const int blocks = static_cast<int>(want < 8LL * sm_count ? want : 8LL * sm_count);
+  const int64_t per_block = 256LL * gemm_bf16::kWidenPer;
+  const int64_t blocks64 = (chunks + per_block - 1) / per_block;
+  if (blocks64 > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  const int blocks = static_cast<int>(blocks64 > 0 ? blocks64 : 1);
   const uint4* codes = reinterpret_cast<const uint4*>(w->values);
   uint4* dst = static_cast<uint4*>(out);
   if (w->kind == SC_WEIGHT_INT8)
@@ -406,6 +500,19 @@ cudaError_t launch_gemm_bf16_peers(const CUtensorMap& tmap_x, const CUtensorMap&
                                    const uint16_t* bias, const PeerOut& peers, int64_t m, int* err, int sm_count,
                                    cudaStream_t stream) {
   return gemm_bf16::launch_gemm<false, true>(tmap_x, tmap_w, w, bias, nullptr, m, err, sm_count, stream, peers);
+}
+
+cudaError_t launch_gemm_bf16_op(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
+                                const uint16_t* bias, void* y, int op, const float* gate, int64_t m, int* err,
+                                int sm_count, cudaStream_t stream) {
+  const PeerOut none = {};
+  if (op == gemm_bf16::kOpGelu)
+    return gemm_bf16::launch_gemm<false, false, gemm_bf16::kOpGelu>(tmap_x, tmap_w, w, bias, y, m, err, sm_count,
+                                                                    stream, none);
+  if (op == gemm_bf16::kOpResidual)
+    return gemm_bf16::launch_gemm<true, false, gemm_bf16::kOpResidual>(tmap_x, tmap_w, w, bias, y, m, err, sm_count,
+                                                                       stream, none, gate);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_gather_wait(const uint32_t* flags, int world, uint32_t epoch, int* err, cudaStream_t stream) {

@@ -142,7 +142,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0, gcount = 0;
       uint32_t phase = 0, issued = 0, last_parity = 0;
       for (int tile = pair; tile < num_tiles && !*abort; tile += pairs) {
-        const int mt = tile % m_tiles, nt = tile / m_tiles;
+        int mt, nt;
+        tile_coords(tile, m_tiles, n_tiles, mt, nt);
         const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM;
         const int col0 = nt * BN + static_cast<int>(rank) * BNH;
         for (int kt = 0; kt < k_tiles; ++kt) {
@@ -221,7 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     const bool vec_ok = (N % 8) == 0, vec4_ok = (N % 4) == 0;
     for (int tile = pair; tile < num_tiles; tile += pairs) {
-      const int mt = tile % m_tiles, nt = tile / m_tiles;
+      int mt, nt;
+      tile_coords(tile, m_tiles, n_tiles, mt, nt);
       const int n0 = nt * BN;
       const int row = mt * 2 * BM + static_cast<int>(rank) * BM + ew * 32 + lane;
       __syncwarp();

@@ -97,6 +97,11 @@ cudaError_t launch_gemm_bf16_peers(const CUtensorMap& tmap_x, const CUtensorMap&
                                    const uint16_t* bias, const PeerOut& peers, int64_t m, int* err, int sm_count,
                                    cudaStream_t stream);
 cudaError_t launch_gather_wait(const uint32_t* flags, int world, uint32_t epoch, int* err, cudaStream_t stream);
+// The bf16-operand pair GEMM with a fused epilogue operation: op 1 = GELU (tanh) before the bf16 store,
+// op 2 = y (fp32) += gate[n] * v in place (the gated residual).
+cudaError_t launch_gemm_bf16_op(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
+                                const uint16_t* bias, void* y, int op, const float* gate, int64_t m, int* err,
+                                int sm_count, cudaStream_t stream);
 
 // The skinny product on the tensor cores (4 < m <= 32): the x tensor map's box rows for m, and the launch.
 int gemm_skinny_box_rows(int64_t m);

@@ -107,6 +107,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // Flags between GPUs (the fused gather): system-scope acquire load and release store.
+// Output-tile order of the persistent GEMMs: groups of kTileGroupRows row tiles, and inside a group
+// the row tile fastest, so that the tiles in flight at one time (one per CTA pair) share a few row
+// blocks of x and a few column blocks of the weight, which stay in L2.  With x larger than L2 (the
+// DiT blocks' 32768-row products) a plain column-major order re-read all of x from HBM once per
+// column block.  Products with at most kTileGroupRows row tiles keep the column-major order.
+constexpr int kTileGroupRows = 16;
+
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mt, int& nt) {
+  const int group = tile / (kTileGroupRows * n_tiles);
+  const int first = group * kTileGroupRows;
+  const int rows = min(m_tiles - first, kTileGroupRows);
+  const int t = tile - first * n_tiles;
+  mt = first + t % rows;
+  nt = t / rows;
+}
+
+// 16-byte global load cached in L2 only (data this kernel also writes: not the read-only path).
+__device__ __forceinline__ float4 ld_cg_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -29,6 +29,11 @@ from . import abi
 from . import dit_abi as dk
 from .products import Context, QuantizedWeight
 
+# The MMDiT block's GELU and gated residuals run inside the epilogue of the product before them
+# (sc_linear_epilogue) for products of at least FUSE_MIN_ROWS rows.
+FUSED_EPILOGUES = True
+FUSE_MIN_ROWS = 1536
+
 
 def quantize_per_channel(w: torch.Tensor):
     """int8 codes and fp32 scales of a [out, in] weight: s = max|w| / 127 per output, q = round(w / s)."""
@@ -53,6 +58,28 @@ class Linear:
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor, workspace=None) -> torch.Tensor:
         return self.weight.linear_ex(x, out, bias=self.bias, workspace=workspace)
+
+    def _fuse(self, rows: int) -> bool:
+        # The fused epilogues run on the widened route, which sc_linear takes from 1536 rows anyway.
+        return FUSED_EPILOGUES and rows >= FUSE_MIN_ROWS
+
+    def gelu(self, x: torch.Tensor, out: torch.Tensor, workspace=None) -> torch.Tensor:
+        """out (bf16) = gelu_tanh(x W^T + b): fused into the product's epilogue from FUSE_MIN_ROWS rows,
+        else the product and sd_gelu_tanh."""
+        if self._fuse(x.shape[0]):
+            return self.weight.linear_epilogue(x, out, abi.EPI_GELU_TANH, bias=self.bias, workspace=workspace)
+        self(x, out, workspace)
+        return dk.gelu_tanh(out)
+
+    def gated_residual(self, x: torch.Tensor, resid: torch.Tensor, gate: torch.Tensor, scratch: torch.Tensor,
+                       workspace=None) -> torch.Tensor:
+        """resid (fp32) += gate * (x W^T + b): fused into the product's epilogue from FUSE_MIN_ROWS rows,
+        else the product into `scratch` (fp32) and sd_gated_residual."""
+        if self._fuse(x.shape[0]):
+            return self.weight.linear_epilogue(x, resid, abi.EPI_GATED_RESIDUAL, bias=self.bias, gate=gate,
+                                               workspace=workspace)
+        self(x, scratch, workspace)
+        return dk.gated_residual(resid, scratch, gate, False, None, 0.0)
 
     def workspace_bytes(self, m: int) -> int:
         return self.weight.workspace_bytes(m)
@@ -237,13 +264,10 @@ class MMDiTBlock:
             rows = x.shape[0]
             y, a, h = b["y"][:rows], b["a"][:rows], b["h"][:rows]
             merged = merged_rows(o, batch, H, joint, off, n, b["merged"][:rows])
-            sw.out(merged, y, ws)
-            dk.gated_residual(x, y, m[2], False, None, self.eps)
+            sw.out.gated_residual(merged, x, m[2], y, ws)
             dk.layer_norm_modulate(x, m[4], m[3], self.eps, a)
-            sw.mlp1(a, h, ws)
-            dk.gelu_tanh(h)
-            sw.mlp2(h, y, ws)
-            dk.gated_residual(x, y, m[5], False, None, self.eps)
+            sw.mlp1.gelu(a, h, ws)
+            sw.mlp2.gated_residual(h, x, m[5], y, ws)
 
     def close(self) -> None:
         for l in self.linears():

@@ -203,6 +203,29 @@ class QuantizedWeight:
                                                  _ptr(workspace), ws_bytes, _stream_ptr(stream)))
         return out
 
+    def epilogue_workspace_bytes(self) -> int:
+        """Workspace of sc_linear_epilogue at any M: the widened weight (sc_workspace_size from 1536 rows)."""
+        return self.workspace_bytes(1536)
+
+    def linear_epilogue(self, x, out, op: int, bias=None, gate=None, workspace=None, stream=None):
+        """sc_linear_epilogue: v = (x . q) * s + bias with the DiT stage `op` fused into the product's
+        epilogue.  EPI_GELU_TANH: out bf16 [M, N] = gelu_tanh(v); EPI_GATED_RESIDUAL: out fp32 [M, N]
+        += gate * v in place (gate fp32 [N]).  M must exceed 128."""
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.shape[1] != self.k:
+            raise SiliconedError(abi.INVALID_ARG, f"x must be a CUDA bf16 [M, {self.k}] tensor")
+        m = x.shape[0]
+        want = torch.bfloat16 if op == abi.EPI_GELU_TANH else torch.float32
+        if out.dtype != want or tuple(out.shape) != (m, self.n) or not out.is_contiguous():
+            raise SiliconedError(abi.INVALID_ARG, f"out must be a contiguous {want} [{m}, {self.n}] tensor")
+        if gate is not None and (gate.dtype != torch.float32 or gate.numel() != self.n or not gate.is_contiguous()):
+            raise SiliconedError(abi.INVALID_ARG, f"gate must be a contiguous fp32 [{self.n}] tensor")
+        if workspace is None:
+            workspace = self.ctx.workspace(self.epilogue_workspace_bytes(), x.device)
+        ws_bytes = workspace.numel() * workspace.element_size()
+        self.ctx.check(self.ctx.lib.sc_linear_epilogue(self.ctx.ptr, self.ptr, _ptr(x), m, _ptr(bias), _ptr(out), op,
+                                                       _ptr(gate), _ptr(workspace), ws_bytes, _stream_ptr(stream)))
+        return out
+
     def linear(self, x, bias=None, out=None, workspace=None, stream=None):
         """y = bf16((x . q) * s + bias), dispatching on M (GEMV for M <= 32, tensor-core GEMM above)."""
         return self._product("sc_linear", x, bias, out, workspace, stream)

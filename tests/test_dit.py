@@ -237,3 +237,92 @@ def test_mmdit_block_matches_fp32_reference():
     assert rel(x_img, refs[1]) <= 1e-2, rel(x_img, refs[1])
     model.close()
     ctx.close()
+
+
+@gpu
+@needs_cuda
+def test_fused_epilogues_agree_with_the_separate_stages():
+    """From 1536 rows the MMDiT block's gated residuals and GELU run in the product's epilogue: the
+    gated residual bit for bit as the product plus sd_gated_residual (both fmaf(gate, v, x)); the GELU
+    within one bf16 rounding of the product's bf16 output run through sd_gelu_tanh (the separate
+    stages round v to bf16 first, which moves gelu by up to 1.2 |v| 2^-8)."""
+    import siliconed_b200.dit as dit
+    from siliconed_b200.products import Context
+    ctx = Context(0)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    lin = dit.Linear(ctx, 1280, 512, g, bias=True)
+    rows = 2048
+    x = torch.randn(rows, 512, generator=g, device="cuda").to(torch.bfloat16)
+    gate = torch.randn(1280, generator=g, device="cuda")
+    resid0 = torch.randn(rows, 1280, generator=g, device="cuda")
+    ws = torch.empty(lin.workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    scratch = torch.empty(rows, 1280, device="cuda")
+    v = lin(x, torch.empty(rows, 1280, device="cuda"), ws)
+    outs = {}
+    try:
+        for fused in (True, False):
+            dit.FUSED_EPILOGUES = fused
+            r = resid0.clone()
+            lin.gated_residual(x, r, gate, scratch, ws)
+            h = torch.empty(rows, 1280, dtype=torch.bfloat16, device="cuda")
+            lin.gelu(x, h, ws)
+            outs[fused] = (r, h)
+    finally:
+        dit.FUSED_EPILOGUES = True
+    torch.cuda.synchronize()
+    assert torch.equal(outs[True][0], outs[False][0])
+    assert not torch.equal(outs[True][0], resid0)
+    hf, hu = outs[True][1].float(), outs[False][1].float()
+    excess = (hf - hu).abs() - (2.0 ** -7 * hu.abs() + 1.2 * 2.0 ** -8 * v.abs() + 1e-6)
+    assert float(excess.max()) <= 0.0
+    lin.close()
+    ctx.close()
+
+
+@gpu
+@needs_cuda
+def test_mmdit_block_with_fused_epilogues_matches_fp32_reference():
+    """The block at 1536 text and 2048 image rows (the fused epilogues' range) against the same fp32
+    reference, its GELU taken on the fp32 product as the fused epilogue does."""
+    from siliconed_b200.dit import MMDiT, rope_table, image_text_positions, timestep_embedding
+    from siliconed_b200.products import Context
+    ctx = Context(0)
+    batch, st, si, d, heads, mlp = 1, 1536, 2048, 256, 2, 512
+    model = MMDiT(ctx, blocks=1, dim=d, heads=heads, mlp=mlp, seed=5)
+    blk = model.blocks[0]
+    g = torch.Generator(device="cuda").manual_seed(6)
+    x_txt = torch.randn(batch * st, d, generator=g, device="cuda")
+    x_img = torch.randn(batch * si, d, generator=g, device="cuda")
+    freqs = rope_table(image_text_positions(st, 64)[: st + si]).cuda()
+    temb = timestep_embedding(0.3)
+    refs = [x_txt.clone(), x_img.clone()]
+    b = model.buffers(batch, st, si)
+    blk.forward(x_txt, x_img, batch, temb, freqs, b)
+    bf = lambda t: t.to(torch.bfloat16).float()
+    streams = [(blk.txt, refs[0], st), (blk.img, refs[1], si)]
+    mods, qs, ks, vs = [], [], [], []
+    off = 0
+    for sw, x, n in streams:
+        m = lin_ref(sw.modulation, temb).reshape(6, d)
+        mods.append(m)
+        a = bf(ln_ref(x) * (1 + m[1]) + m[0])
+        qkv = bf(lin_ref(sw.qkv, a)).reshape(batch, n, 3, heads, 128).permute(2, 0, 3, 1, 4)
+        f = freqs[off:off + n]
+        qs.append(bf(rope_ref(rms_ref(qkv[0], sw.norm_q, 1e-6), f)))
+        ks.append(bf(rope_ref(rms_ref(qkv[1], sw.norm_k, 1e-6), f)))
+        vs.append(qkv[2])
+        off += n
+    o = bf(attn_ref(torch.cat(qs, 2), torch.cat(ks, 2), torch.cat(vs, 2)))
+    off = 0
+    for (sw, x, n), m in zip(streams, mods):
+        on = o[:, :, off:off + n].permute(0, 2, 1, 3).reshape(batch * n, d)
+        x += m[2] * lin_ref(sw.out, on)
+        a = bf(ln_ref(x) * (1 + m[4]) + m[3])
+        h = lin_ref(sw.mlp1, a)
+        h = bf(0.5 * h * (1 + torch.tanh(math.sqrt(2 / math.pi) * (h + 0.044715 * h ** 3))))
+        x += m[5] * lin_ref(sw.mlp2, h)
+        off += n
+    assert rel(x_txt, refs[0]) <= 1e-2, rel(x_txt, refs[0])
+    assert rel(x_img, refs[1]) <= 1e-2, rel(x_img, refs[1])
+    model.close()
+    ctx.close()

@@ -350,7 +350,9 @@ def test_errors_are_statuses(ctx):
 
 @pytest.mark.parametrize("kind,m,k,n", [(abi.WEIGHT_INT8, 256, 3072, 3072), (abi.WEIGHT_INT8, 600, 4096, 1000),
                                         (abi.WEIGHT_INT8, 4096, 512, 3072), (abi.WEIGHT_E4M3, 384, 2048, 2560),
-                                        (abi.WEIGHT_INT8, 2304, 256, 5000), (abi.WEIGHT_E4M3, 1600, 1024, 1000)])
+                                        (abi.WEIGHT_INT8, 2304, 256, 5000), (abi.WEIGHT_E4M3, 1600, 1024, 1000),
+                                        # more than 16 row tiles: grouped tile order, ragged last group
+                                        (abi.WEIGHT_INT8, 9000, 256, 1288), (abi.WEIGHT_E4M3, 4500, 512, 776)])
 def test_linear_more_shapes_match_oracle(ctx, kind, m, k, n):
     g = np.random.default_rng(m + k + n)
     x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
@@ -367,7 +369,8 @@ def test_linear_more_shapes_match_oracle(ctx, kind, m, k, n):
     check_against_oracle(ctx, kind, x, q, s, b, f"shape {m}x{k}x{n}")
 
 
-@pytest.mark.parametrize("kind,m,k,n", [(abi.WEIGHT_INT8, 600, 4096, 1000), (abi.WEIGHT_E4M3, 384, 2048, 2560)])
+@pytest.mark.parametrize("kind,m,k,n", [(abi.WEIGHT_INT8, 600, 4096, 1000), (abi.WEIGHT_E4M3, 384, 2048, 2560),
+                                        (abi.WEIGHT_INT8, 4500, 256, 1288)])
 def test_fused_pair_kernel_matches_oracle(ctx, kind, m, k, n):
     """The fused pair kernel (no workspace: codes converted in shared memory) on its own."""
     g = np.random.default_rng(m * 3 + n)
@@ -478,3 +481,100 @@ def test_config2_full_size(ctx):
 def test_config4_full_size(ctx, m, nk):
     e32, e16, mx = sampled_check(ctx, configs.config4(m, *nk), rows=m)
     assert e32 <= REL_L2_F32 and e16 <= REL_L2_BF16 and mx <= MAX_ABS_BF16, (m, nk, e32, e16, mx)
+
+
+# ---------------------------------------------------------------------------------------------
+# sc_linear_epilogue: the DiT block's GELU and gated residual fused into the product's epilogue
+
+
+def gelu_tanh64(v: np.ndarray) -> np.ndarray:
+    v = v.astype(np.float64)
+    return 0.5 * v * (1.0 + np.tanh(0.7978845608028654 * (v + 0.044715 * v ** 3)))
+
+
+def linear_epilogue(ctx, w, x_dev, m, bias_dev, y, op, gate=None, ws_bytes=None):
+    need = w.workspace_bytes(1536) if ws_bytes is None else ws_bytes
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    return ctx.lib.sc_linear_epilogue(ctx.ptr, w.ptr, ctypes.c_void_p(x_dev.data_ptr()), m,
+                                      ctypes.c_void_p(bias_dev.data_ptr() if bias_dev is not None else 0),
+                                      ctypes.c_void_p(y.data_ptr()), op,
+                                      ctypes.c_void_p(gate.data_ptr() if gate is not None else 0),
+                                      ctypes.c_void_p(ws.data_ptr()), need, ctypes.c_void_p(st))
+
+
+@pytest.mark.parametrize("kind,m,k,n", [(abi.WEIGHT_INT8, 1600, 3072, 3072),
+                                        (abi.WEIGHT_INT8, 200, 512, 700),
+                                        (abi.WEIGHT_E4M3, 2048, 1024, 2304)])
+def test_fused_epilogues_match_the_unfused_stages(ctx, kind, m, k, n):
+    """GELU: within one bf16 rounding of gelu_tanh (fp64) of the route's fp32 output v; gated
+    residual: fmaf(gate, v, x) bit for bit (fp64 product plus add, one rounding to fp32, allowed one
+    fp32 ulp where the fp64 sum rounds twice); both against the oracle's fp32 product through v."""
+    g = np.random.default_rng(5 * m + n)
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    s = (np.abs(g.standard_normal(n)) * 2e-4 + 1e-6).astype(np.float32)
+    bias = configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.1)
+    if kind == abi.WEIGHT_INT8:
+        q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+        c_ref, _ = oracle.linear_int8(x, q.view(np.int8), s, bias)
+    else:
+        q = configs.to_e4m3_codes(g.standard_normal((k, n), dtype=np.float32) * 4)
+        q[(q & 0x7F) == 0x7F] ^= 1
+        wf = oracle.dequantize(q, oracle.E4M3, s, oracle.SCALE_F32, oracle.LAYOUT_COLUMNS, n).reshape(k, n)
+        c_ref, _ = oracle.linear_widened(x, wf, bias)
+    w = QuantizedWeight(ctx, q, kind, s)
+    xd, bd = bf16_dev(x), bf16_dev(bias)
+    # v: the same operands and summation order as the fused epilogues (the widened route's fp32 output
+    # where m >= 1536; the fused pair kernel's below it, the same bits).
+    v = host(linear_ex(ctx, w, xd, m, bd, True, True))
+    assert rel_l2(v, c_ref) <= REL_L2_F32
+    h = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    ctx.check(linear_epilogue(ctx, w, xd, m, bd, h, abi.EPI_GELU_TANH))
+    ctx.poll_errors()
+    hf = f32_of_bf16(bf16_host(h)).astype(np.float64)
+    ref = gelu_tanh64(v)
+    # the bf16 rounding, plus 2^-10 of it for the epilogue's exp-and-divide form of tanh (~2e-6 relative)
+    bound = 2.0 ** -8 * (1.0 + 2.0 ** -10) * np.abs(ref) + np.abs(v) * 2.0 ** -20 + 1e-30
+    assert float((np.abs(hf - ref) - bound).max()) <= 0.0, "GELU epilogue beyond one bf16 rounding"
+    hr = f32_of_bf16(configs.to_bf16_bits(gelu_tanh64(c_ref).astype(np.float32)))
+    assert rel_l2(hf, hr) <= REL_L2_BF16
+    # one bf16 ulp, the fp32 cancellation in 1 + tanh where v is large and negative, and the spread of
+    # a change of fp32 summation order (as in check_against_oracle) times max |gelu'| < 1.2
+    wf = oracle.dequantize(q, kind, s, oracle.SCALE_F32, oracle.LAYOUT_COLUMNS, n).reshape(k, n)
+    xf = torch.from_numpy(f32_of_bf16(x))
+    spread = torch.sqrt((xf * xf) @ torch.from_numpy(wf * wf)).numpy().astype(np.float64)
+    bound = 2.0 ** -7 * np.abs(hr) + 2.0 ** -20 * np.abs(c_ref) + 1.2 * 8.0 * np.sqrt(k) * 2.0 ** -24 * spread + 1e-9
+    assert float((np.abs(hf - hr) - bound).max()) <= 0.0, "more than one bf16 ulp"
+    # gated residual, in place on an fp32 stream
+    x0 = g.standard_normal((m, n), dtype=np.float32)
+    gate = (g.standard_normal(n, dtype=np.float32) * 0.5).astype(np.float32)
+    resid = dev(x0.copy())
+    ctx.check(linear_epilogue(ctx, w, xd, m, bd, resid, abi.EPI_GATED_RESIDUAL, dev(gate)))
+    ctx.poll_errors()
+    got = host(resid)
+    want = (gate.astype(np.float64) * v.astype(np.float64) + x0.astype(np.float64)).astype(np.float32)
+    ulps = np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64))
+    assert int(ulps.max()) <= 1 and float(np.mean(ulps == 0)) >= 0.999, "gated residual is not fmaf(gate, v, x)"
+    want_oracle = x0.astype(np.float64) + gate.astype(np.float64) * c_ref.astype(np.float64)
+    assert rel_l2(got - x0, want_oracle - x0) <= REL_L2_F32
+    w.close()
+
+
+def test_fused_epilogue_guards(ctx):
+    g = np.random.default_rng(3)
+    k, n = 256, 512
+    q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+    w = QuantizedWeight(ctx, q, abi.WEIGHT_INT8, np.full(n, 1e-3, np.float32))
+    x128 = bf16_dev(configs.to_bf16_bits(g.standard_normal((128, k), dtype=np.float32)))
+    x256 = bf16_dev(configs.to_bf16_bits(g.standard_normal((256, k), dtype=np.float32)))
+    h = torch.empty((256, n), dtype=torch.bfloat16, device="cuda")
+    r = torch.zeros((256, n), dtype=torch.float32, device="cuda")
+    gate = torch.ones(n, dtype=torch.float32, device="cuda")
+    assert linear_epilogue(ctx, w, x128, 128, None, h, abi.EPI_GELU_TANH) == abi.UNSUPPORTED_SHAPE
+    assert linear_epilogue(ctx, w, x256, 256, None, h, abi.EPI_GELU_TANH, ws_bytes=1024) == abi.WORKSPACE_TOO_SMALL
+    assert linear_epilogue(ctx, w, x256, 256, None, r, abi.EPI_GATED_RESIDUAL) == abi.INVALID_ARG
+    assert linear_epilogue(ctx, w, x256, 256, None, h, 7) == abi.INVALID_ARG
+    assert linear_epilogue(ctx, w, x256, 0, None, h, abi.EPI_GELU_TANH) == abi.OK
+    ctx.check(linear_epilogue(ctx, w, x256, 256, None, r, abi.EPI_GATED_RESIDUAL, gate))
+    ctx.poll_errors()
+    w.close()
