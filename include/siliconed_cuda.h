@@ -110,6 +110,28 @@ SC_API sc_status sc_weight_create_shard(sc_ctx* ctx, const void* values, sc_weig
 
 SC_API sc_status sc_weight_destroy(sc_ctx* ctx, sc_weight* w);
 
+/*
+ * Marks an int8 weight as ComfyUI's convrot (Artifact.rotation, Artifact.swift:397-411): the published
+ * weight is W = (q . s) . R along K, R block-diagonal with blocks H / sqrt(G), H the regular Hadamard of
+ * size G (Kronecker powers of [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],[-1,1,1,1]]), G a power of 4 from 4 to 256
+ * dividing K.  From then on every product rotates its activation first, x . W = (x . R) . q . s
+ * (TensorGEMM.swift:53-54, rotate_groups :183-201): in fp32 butterflies, rounded to bf16, into the front
+ * of the caller's workspace (sc_workspace_size grows by m * k * 2 bytes, rounded up to 256), and
+ * sc_dequantize exports float(H . q) * (s / sqrt(G)) (Widen.dequantizeRotated, Widen.swift:374-428).
+ * group 0 clears the mark.  SC_INVALID_ARG for an e4m3 weight, SC_UNSUPPORTED_SHAPE for another group or
+ * K not a multiple of it, SC_REFUSED when a nonzero scale over sqrt(G) is subnormal (the smallest
+ * rotated product; QuantizedLayouts.checkSubnormal).
+ */
+SC_API sc_status sc_weight_set_rotation(sc_ctx* ctx, sc_weight* w, int group);
+
+/*
+ * out[m, k] = bf16(x . R) for bf16 x [m, k]: the activation's rotation of a convrot product on its own
+ * (rotate_groups, TensorGEMM.swift:183-201: fp32 butterflies of spans 1, 4, 16, 64, then times
+ * 1/sqrt(G), then nearest-even to bf16).  K a multiple of the group and of 8; x and out 16-byte aligned.
+ */
+SC_API sc_status sc_rotate_activation(sc_ctx* ctx, const sc_bf16* x, int64_t m, int64_t k, int group, sc_bf16* out,
+                                      void* stream);
+
 /* Shape, kind and device bytes of a registered weight (any out pointer may be NULL). */
 SC_API sc_status sc_weight_info(const sc_weight* w, int64_t* k, int64_t* n, int* kind, size_t* device_bytes);
 

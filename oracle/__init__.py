@@ -58,6 +58,8 @@ def lib() -> ctypes.CDLL:
         L.orc_linear_fp64.argtypes = [P, I64, I64, I64, P, P, P]
         L.orc_gemv_int8_splits.argtypes = [P, I64, I64, P, P, I64, P, P]
         L.orc_set_threads.argtypes = [I]
+        L.orc_rotate_groups_bf16.argtypes = [P, I64, I64, I, P]
+        L.orc_dequantize_rotated.argtypes = [P, I64, I64, I, P, P]
         L.orc_max_threads.restype = I
         _lib = L
     return _lib
@@ -153,3 +155,24 @@ def gemv_int8_splits(x: np.ndarray, q_kn: np.ndarray, s: np.ndarray, splits: int
     out = np.empty(n, np.float32)
     lib().orc_gemv_int8_splits(_p(x), k, n, _p(q), _p(s), splits, _p(parts), _p(out))
     return parts, out
+
+
+def rotate_groups_bf16(x_bf16: np.ndarray, group: int) -> np.ndarray:
+    """convrot on the activation (rotate_groups, TensorGEMM.swift:183-201): bf16 [m, k] -> bf16 [m, k]."""
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    m, k = x.shape
+    assert k % group == 0
+    out = np.empty_like(x)
+    lib().orc_rotate_groups_bf16(_p(x), m, k, group, _p(out))
+    return out
+
+
+def dequantize_rotated(q_kn: np.ndarray, group: int, s: np.ndarray) -> np.ndarray:
+    """Widen.dequantizeRotated (Widen.swift:374-428): fp32 [k, n] = float(H q) * (s / sqrt(G))."""
+    q = np.ascontiguousarray(q_kn, np.int8)
+    k, n = q.shape
+    assert k % group == 0
+    s = np.ascontiguousarray(np.broadcast_to(np.asarray(s, np.float32), (n,)), np.float32)
+    out = np.empty((k, n), np.float32)
+    lib().orc_dequantize_rotated(_p(q), k, n, group, _p(s), _p(out))
+    return out

@@ -198,6 +198,70 @@ void orc_gemv_int8_splits(const float* x, int64_t k, int64_t n, const int8_t* q,
     }
 }
 
+/* TensorGEMM.swift:183-201 (rotate_groups), operation for operation, on fp32 values. */
+static void rotate_group_f32(float* v, int g) {
+    for (int span = 1; span < g; span *= 4) {
+        for (int t = 0; t < g / 4; ++t) {
+            const int j = (t / span) * 4 * span + t % span;
+            const float a = v[j], b = v[j + span], c = v[j + 2 * span], d = v[j + 3 * span];
+            const float p = a + b, mm = a - b, u = c + d, w = c - d;
+            v[j] = p + w;
+            v[j + span] = p - w;
+            v[j + 2 * span] = mm + u;
+            v[j + 3 * span] = u - mm;
+        }
+    }
+}
+
+static float rotation_norm(int g) {
+    int p = 0;
+    while ((1 << (2 * p)) < g) ++p;          /* g = 4^p, sqrt(g) = 2^p */
+    return ldexpf(1.0f, -p);
+}
+
+void orc_rotate_groups_bf16(const uint16_t* x, int64_t m, int64_t k, int group, uint16_t* out) {
+    const float norm = rotation_norm(group);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < m; ++r) {
+        float v[256];
+        for (int64_t g0 = 0; g0 < k; g0 += group) {
+            for (int i = 0; i < group; ++i) v[i] = orc_bf16_to_f32(x[r * k + g0 + i]);
+            rotate_group_f32(v, group);
+            for (int i = 0; i < group; ++i) out[r * k + g0 + i] = orc_f32_to_bf16(v[i] * norm);
+        }
+    }
+}
+
+/* Widen.hadamard (Widen.swift:550-566): m <- H . m, exact in int32. */
+static void hadamard_i32(int32_t* v, int g) {
+    for (int span = 1; span < g; span *= 4) {
+        for (int base = 0; base < g; base += 4 * span) {
+            for (int j = base; j < base + span; ++j) {
+                const int32_t a = v[j], b = v[j + span], c = v[j + 2 * span], d = v[j + 3 * span];
+                const int32_t p = a + b, mm = a - b, u = c + d, w = c - d;
+                v[j] = p + w;
+                v[j + span] = p - w;
+                v[j + 2 * span] = mm + u;
+                v[j + 3 * span] = u - mm;
+            }
+        }
+    }
+}
+
+void orc_dequantize_rotated(const int8_t* q, int64_t k, int64_t n, int group, const float* s, float* out) {
+    const float norm = rotation_norm(group);
+#pragma omp parallel for schedule(static)
+    for (int64_t j = 0; j < n; ++j) {
+        int32_t v[256];
+        const float factor = s[j] * norm;    /* exact: a power of two */
+        for (int64_t g0 = 0; g0 < k; g0 += group) {
+            for (int i = 0; i < group; ++i) v[i] = q[(g0 + i) * n + j];
+            hadamard_i32(v, group);
+            for (int i = 0; i < group; ++i) out[(g0 + i) * n + j] = (float)v[i] * factor;
+        }
+    }
+}
+
 void orc_set_threads(int threads) {
 #ifdef _OPENMP
     if (threads > 0) omp_set_num_threads(threads);

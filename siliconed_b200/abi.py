@@ -47,6 +47,8 @@ SIGNATURES = {
     "sc_linear": (_I, [_P, _P, _P, _I64, _P, _P, _P, _SZ, _P]),
     "sc_linear_ex": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _SZ, _P]),
     "sc_linear_epilogue": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _P, _SZ, _P]),
+    "sc_weight_set_rotation": (_I, [_P, _P, _I]),
+    "sc_rotate_activation": (_I, [_P, _P, _I64, _I64, _I, _P, _P]),
     "sc_linear_ex_noalloc": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P]),
     "sc_linear_allgather": (_I, [_P, _P, _P, _I64, _P, _P, _P, _I, _I, _I64, _I64, ctypes.c_uint32, _P, _SZ, _P]),
     "sc_allgather_wait": (_I, [_P, _P, _I, ctypes.c_uint32, _P]),

@@ -151,6 +151,23 @@ sc_status check_product_args(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, 
   return SC_OK;
 }
 
+// A convrot weight: x . W = (x . R) . q . s, so x is rotated into the front of the workspace first; on
+// return x, workspace and workspace_bytes describe the product's operand and the rest of the scratch.
+sc_status rotate_operand(sc_ctx* ctx, const sc_weight* w, const sc_bf16*& x, int64_t m, void*& workspace,
+                         size_t& workspace_bytes, cudaStream_t st) {
+  if (w->rotation == 0 || m == 0) return SC_OK;
+  const size_t rx = rotated_x_bytes(m, w->k);
+  if (workspace == nullptr || workspace_bytes < rx || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(ctx, SC_WORKSPACE_TOO_SMALL, "a convrot weight needs a 256-byte aligned workspace (sc_workspace_size)");
+  sc_bf16* xr = static_cast<sc_bf16*>(workspace);
+  sc_status s = check_cuda(ctx, launch_rotate(x, m, w->k, w->rotation, xr, st), "rotation launch");
+  if (s != SC_OK) return s;
+  x = xr;
+  workspace_bytes -= rx;
+  workspace = workspace_bytes > 0 ? static_cast<uint8_t*>(workspace) + rx : nullptr;
+  return SC_OK;
+}
+
 sc_status run_gemv(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, void* y,
                    bool f32_out, void* workspace, size_t workspace_bytes, cudaStream_t st) {
   const size_t need = gemv_workspace_bytes(w, m, ctx->sm_count);
@@ -170,6 +187,7 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
   if (m == 0) return SC_OK;
   if ((s = enter(ctx)) != SC_OK) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((s = rotate_operand(ctx, w, x, m, workspace, workspace_bytes, st)) != SC_OK) return s;
   if (m <= kSkinnyMinRows) return run_gemv(ctx, w, x, m, bias, y, f32_out, workspace, workspace_bytes, st);
   CUtensorMap tmx;
   if (m <= 32) {
@@ -325,6 +343,10 @@ sc_status sc_weight_create_shard(sc_ctx* ctx, const void* values, sc_weight_kind
   std::vector<float> sf(static_cast<size_t>(w->n_pad), 0.0f);
   for (int64_t j = 0; j < cols; ++j)
     sf[static_cast<size_t>(j)] = scale_to_f32(sbytes.data(), scale_type, layout == SC_SCALE_TENSOR ? 0 : n_begin + j);
+  for (int64_t j = 0; j < cols; ++j) {
+    const float a = std::fabs(sf[static_cast<size_t>(j)]);
+    if (a != 0.0f && (w->min_abs_scale == 0.0f || a < w->min_abs_scale)) w->min_abs_scale = a;
+  }
 
   const size_t vbytes = static_cast<size_t>(w->n_pad * w->k_pad);
   const size_t soff = static_cast<size_t>(round_up(static_cast<int64_t>(vbytes), 256));
@@ -411,7 +433,45 @@ sc_status sc_dequantize(sc_ctx* ctx, const sc_weight* w, float* out, void* strea
   if (!is_device_pointer(out)) return fail(ctx, SC_INVALID_ARG, "out must be device (or managed) memory");
   sc_status s = enter(ctx);
   if (s != SC_OK) return s;
+  if (w->rotation != 0)
+    return check_cuda(ctx, launch_dequantize_rotated(w, out, static_cast<cudaStream_t>(stream)),
+                      "rotated dequantize launch");
   return check_cuda(ctx, launch_dequantize(w, out, static_cast<cudaStream_t>(stream)), "dequantize launch");
+}
+
+sc_status sc_weight_set_rotation(sc_ctx* ctx, sc_weight* w, int group) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (w == nullptr) return fail(ctx, SC_INVALID_ARG, "null weight");
+  if (group == 0) {
+    w->rotation = 0;
+    return SC_OK;
+  }
+  if (w->kind != SC_WEIGHT_INT8) return fail(ctx, SC_INVALID_ARG, "convrot is read on int8 weights only");
+  if (!is_rotation_group(group))
+    return fail(ctx, SC_UNSUPPORTED_SHAPE, "convrot group must be a power of 4 from 4 to 256");
+  if (w->k % group != 0) return fail(ctx, SC_UNSUPPORTED_SHAPE, "K must be a multiple of the convrot group");
+  int p = 0;
+  while ((1 << (2 * p)) < group) ++p;
+  if (w->min_abs_scale != 0.0f && std::ldexp(w->min_abs_scale, -p) < FLT_MIN)
+    return fail(ctx, SC_REFUSED, "a scale over sqrt(G) is subnormal: its rotated products can fall below 2^-126");
+  w->rotation = group;
+  return SC_OK;
+}
+
+sc_status sc_rotate_activation(sc_ctx* ctx, const sc_bf16* x, int64_t m, int64_t k, int group, sc_bf16* out,
+                               void* stream) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (m < 0 || k <= 0) return fail(ctx, SC_INVALID_ARG, "m < 0 or k <= 0");
+  if (!is_rotation_group(group)) return fail(ctx, SC_UNSUPPORTED_SHAPE, "group must be a power of 4 from 4 to 256");
+  if (k % group != 0 || k % 8 != 0) return fail(ctx, SC_UNSUPPORTED_SHAPE, "K must be a multiple of the group and of 8");
+  if (m == 0) return SC_OK;
+  if (x == nullptr || out == nullptr) return fail(ctx, SC_INVALID_ARG, "null x or out");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(ctx, SC_UNALIGNED, "x and out must be 16-byte aligned");
+  if (!is_device_pointer(x) || !is_device_pointer(out)) return fail(ctx, SC_INVALID_ARG, "x and out must be device memory");
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  return check_cuda(ctx, launch_rotate(x, m, k, group, out, static_cast<cudaStream_t>(stream)), "rotation launch");
 }
 
 sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* bytes) {
@@ -420,6 +480,7 @@ sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* 
   if (m >= 1 && m <= 32) *bytes = gemv_workspace_bytes(w, m, ctx->sm_count);
   else if (m >= kWidenMinRows) *bytes = widened_bytes(w);
   else *bytes = 0;
+  if (w->rotation != 0 && m >= 1) *bytes += rotated_x_bytes(m, w->k);  // the rotated x comes first
   return SC_OK;
 }
 
@@ -446,10 +507,13 @@ sc_status sc_linear_epilogue(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, 
     return fail(ctx, SC_INVALID_ARG, "the gated residual needs a 4-byte aligned device gate of n floats");
   if (m == 0) return SC_OK;
   if (m <= kPairMinRows) return fail(ctx, SC_UNSUPPORTED_SHAPE, "sc_linear_epilogue takes more than 128 rows");
-  if (workspace == nullptr || workspace_bytes < widened_bytes(w) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
-    return fail(ctx, SC_WORKSPACE_TOO_SMALL, "sc_linear_epilogue needs a 256-byte aligned workspace of n_pad * k_pad * 2 bytes");
+  const size_t rx = w->rotation != 0 ? rotated_x_bytes(m, w->k) : 0;
+  if (workspace == nullptr || workspace_bytes < rx + widened_bytes(w) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(ctx, SC_WORKSPACE_TOO_SMALL,
+                "sc_linear_epilogue needs a 256-byte aligned workspace of n_pad * k_pad * 2 bytes (+ the rotated x)");
   if ((s = enter(ctx)) != SC_OK) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((s = rotate_operand(ctx, w, x, m, workspace, workspace_bytes, st)) != SC_OK) return s;
   CUtensorMap tmx, tmw;
   if ((s = make_tmap_x(ctx, x, m, w->k, &tmx)) != SC_OK) return s;
   if ((s = make_tmap_widened(ctx, w, workspace, &tmw)) != SC_OK) return s;
@@ -476,7 +540,9 @@ sc_status sc_gemv_w8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
   if (m > 32) return fail(ctx, SC_UNSUPPORTED_SHAPE, "sc_gemv_w8 takes at most 32 rows");
   if (m == 0) return SC_OK;
   if ((s = enter(ctx)) != SC_OK) return s;
-  return run_gemv(ctx, w, x, m, bias, y, false, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((s = rotate_operand(ctx, w, x, m, workspace, workspace_bytes, st)) != SC_OK) return s;
+  return run_gemv(ctx, w, x, m, bias, y, false, workspace, workspace_bytes, st);
 }
 
 sc_status sc_linear_allgather(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
@@ -502,8 +568,10 @@ sc_status sc_linear_allgather(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x,
     peers.y[r] = y_peers[r];
     peers.flags[r] = flag_peers[r];
   }
-  if (workspace == nullptr || workspace_bytes < widened_bytes(w) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
-    return fail(ctx, SC_WORKSPACE_TOO_SMALL, "the fused gather needs a 256-byte aligned workspace of n_pad * k_pad * 2 bytes");
+  const size_t rx = w->rotation != 0 ? rotated_x_bytes(m, w->k) : 0;
+  if (workspace == nullptr || workspace_bytes < rx + widened_bytes(w) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(ctx, SC_WORKSPACE_TOO_SMALL,
+                "the fused gather needs a 256-byte aligned workspace of n_pad * k_pad * 2 bytes (+ the rotated x)");
   peers.world = world;
   peers.rank = rank;
   peers.col0 = col0;
@@ -513,6 +581,7 @@ sc_status sc_linear_allgather(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x,
   sc_status s = enter(ctx);
   if (s != SC_OK) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((s = rotate_operand(ctx, w, x, m, workspace, workspace_bytes, st)) != SC_OK) return s;
   CUtensorMap tmx, tmw;
   if ((s = make_tmap_x(ctx, x, m, w->k, &tmx)) != SC_OK) return s;
   if ((s = make_tmap_widened(ctx, w, workspace, &tmw)) != SC_OK) return s;

@@ -44,6 +44,8 @@ struct sc_weight {
   float* scales = nullptr;    // [n_pad] fp32 (0 in the padding)
   size_t bytes = 0;
   bool has_nan_codes = false; // e4m3 weight holding NaN codes (0x7F / 0xFF)
+  float min_abs_scale = 0.0f; // the smallest nonzero |s| (0 if every scale is 0)
+  int rotation = 0;           // convrot group G (0: none): products rotate x first (sc_rotate.cu)
   int device = -1;
   CUtensorMap tmap_values;    // 2D map over values: inner K (bytes), outer N rows; box 64 x 256
   CUtensorMap tmap_values_half;  // the same, box 64 x 128 (the half tile one CTA of a pair converts)
@@ -61,6 +63,12 @@ cudaError_t launch_retile(const uint8_t* src, bool published_nk, int kind, int64
                           int64_t n_cols, uint8_t* dst, int64_t k_pad, int64_t n_pad, int* nan_flag,
                           cudaStream_t stream);
 cudaError_t launch_dequantize(const sc_weight* w, float* out, cudaStream_t stream);
+// convrot (sc_rotate.cu): G a power of 4 in [4, 256]; the rotated activation's scratch; the rotation of
+// x [m, k] bf16 into out; the rotated weight's fp32 export.
+bool is_rotation_group(int64_t g);
+size_t rotated_x_bytes(int64_t m, int64_t k);
+cudaError_t launch_rotate(const uint16_t* x, int64_t m, int64_t k, int group, uint16_t* out, cudaStream_t stream);
+cudaError_t launch_dequantize_rotated(const sc_weight* w, float* out, cudaStream_t stream);
 
 cudaError_t launch_gemm_tc(const CUtensorMap& tmap_x, const sc_weight* w, const uint16_t* bias, void* y, bool f32_out,
                            int64_t m, int* err, int sm_count, cudaStream_t stream);

@@ -104,7 +104,7 @@ class QuantizedWeight:
     """
 
     def __init__(self, ctx: Context, values, kind: int, scales, *, scale_type: int | None = None,
-                 published_nk: bool = False, columns: tuple[int, int] | None = None, stream=None):
+                 published_nk: bool = False, columns: tuple[int, int] | None = None, rotation: int = 0, stream=None):
         self.ctx = ctx
         lib = ctx.lib
         on_device = torch is not None and isinstance(values, torch.Tensor) and values.is_cuda
@@ -147,6 +147,15 @@ class QuantizedWeight:
         ctx.check(lib.sc_weight_info(self.ptr, ctypes.byref(bk), ctypes.byref(bn), ctypes.byref(kd),
                                      ctypes.byref(by)))
         self.device_bytes = int(by.value)
+        self.rotation = 0
+        if rotation:
+            self.set_rotation(rotation)
+
+    def set_rotation(self, group: int) -> None:
+        """ComfyUI's convrot of group G on this int8 weight (sc_weight_set_rotation; 0 clears it): the
+        products rotate x first, the export is float(H q) * s / sqrt(G)."""
+        self.ctx.check(self.ctx.lib.sc_weight_set_rotation(self.ctx.ptr, self.ptr, int(group)))
+        self.rotation = int(group)
 
     def close(self) -> None:
         if getattr(self, "ptr", None):
@@ -203,9 +212,10 @@ class QuantizedWeight:
                                                  _ptr(workspace), ws_bytes, _stream_ptr(stream)))
         return out
 
-    def epilogue_workspace_bytes(self) -> int:
-        """Workspace of sc_linear_epilogue at any M: the widened weight (sc_workspace_size from 1536 rows)."""
-        return self.workspace_bytes(1536)
+    def epilogue_workspace_bytes(self, m: int) -> int:
+        """Workspace of sc_linear_epilogue for M rows: the widened weight (sc_workspace_size from 1536 rows),
+        after the rotated x of a convrot weight."""
+        return self.workspace_bytes(max(int(m), 1536))
 
     def linear_epilogue(self, x, out, op: int, bias=None, gate=None, workspace=None, stream=None):
         """sc_linear_epilogue: v = (x . q) * s + bias with the DiT stage `op` fused into the product's
@@ -220,7 +230,7 @@ class QuantizedWeight:
         if gate is not None and (gate.dtype != torch.float32 or gate.numel() != self.n or not gate.is_contiguous()):
             raise SiliconedError(abi.INVALID_ARG, f"gate must be a contiguous fp32 [{self.n}] tensor")
         if workspace is None:
-            workspace = self.ctx.workspace(self.epilogue_workspace_bytes(), x.device)
+            workspace = self.ctx.workspace(self.epilogue_workspace_bytes(m), x.device)
         ws_bytes = workspace.numel() * workspace.element_size()
         self.ctx.check(self.ctx.lib.sc_linear_epilogue(self.ctx.ptr, self.ptr, _ptr(x), m, _ptr(bias), _ptr(out), op,
                                                        _ptr(gate), _ptr(workspace), ws_bytes, _stream_ptr(stream)))
@@ -232,6 +242,17 @@ class QuantizedWeight:
 
     def gemv(self, x, bias=None, out=None, workspace=None, stream=None):
         return self._product("sc_gemv_w8", x, bias, out, workspace, stream)
+
+
+def rotate_activation(ctx: Context, x, group: int, out=None, stream=None):
+    """sc_rotate_activation: bf16 [M, K] -> bf16(x . H / sqrt(G)) per group of G along K (rotate_groups)."""
+    if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or not x.is_contiguous():
+        raise SiliconedError(abi.INVALID_ARG, "x must be a contiguous CUDA bf16 [M, K] tensor")
+    if out is None:
+        out = torch.empty_like(x)
+    ctx.check(ctx.lib.sc_rotate_activation(ctx.ptr, _ptr(x), x.shape[0], x.shape[1], int(group), _ptr(out),
+                                           _stream_ptr(stream)))
+    return out
 
 
 class WeightProducts:

@@ -148,3 +148,58 @@ def test_linear_routes_against_fp64():
     assert worst < 1e-5, worst
     c64 = oracle.linear_fp64(x, w, b)
     assert np.allclose(c64, g["e4m3_exact"], rtol=1e-12, atol=1e-12)
+
+
+# ---------------------------------------------------------------------------------------------
+# convrot (ComfyUI's rotated int8 maps): DequantizeTests.swift:159-214 restated
+
+
+def regular_hadamard(g: int) -> np.ndarray:
+    """The unnormalized regular Hadamard of size g by Kronecker powers of H4, built independently of
+    the butterflies (as comfy_kitchen's _build_hadamard; DequantizeTests.swift:159-172)."""
+    h4 = np.array([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]], np.int64)
+    h = h4
+    while h.shape[0] < g:
+        h = np.kron(h, h4)
+    return h
+
+
+@pytest.mark.parametrize("g,k,n", [(256, 768, 328), (256, 256, 12), (64, 192, 136), (16, 64, 40), (4, 8, 20),
+                                   (16, 32, 8200), (4, 8, 4100)])
+def test_dequantize_rotated_is_exactly_rotated(g, k, n):
+    """Float(H q) * (s / sqrt(G)) at the bit (Widen.dequantizeRotated), with columns of +-127 / -128
+    following H's first row (the extremes of m), bf16- and fp32-valued scales, one scale for the tensor."""
+    rng = np.random.default_rng(g * 1000 + n)
+    q = rng.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8)
+    h = regular_hadamard(g)
+    q[:g, 0] = np.where(h[0] > 0, 127, -128)
+    q[:g, 1] = np.where(h[0] > 0, -128, 127)
+    m = np.empty((k, n), np.int64)
+    for g0 in range(0, k, g):
+        m[g0:g0 + g] = h @ q[g0:g0 + g].astype(np.int64)
+    assert np.abs(m).max() <= 32648
+    norm = np.float32(1.0 / np.sqrt(g))
+    s32 = (np.abs(rng.standard_normal(n)) * 1e-3 + 1e-6).astype(np.float32)
+    for s in (s32, oracle.bf16_to_f32(oracle.f32_to_bf16(s32)), np.full(n, s32[0], np.float32)):
+        got = oracle.dequantize_rotated(q, g, s)
+        want = m.astype(np.float32) * (s * norm)          # one fp32 multiply (s * norm is exact)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"G {g}, [{k}, {n}]"
+
+
+def test_rotate_groups_is_the_orthogonal_rotation():
+    """The fp32 butterflies of rotate_groups against x . H / sqrt(G) in fp64: the bf16 results agree
+    except where the fp32 sum sits within its rounding error of a bf16 tie; rotating twice gives x back
+    (H / sqrt(G) is symmetric and orthogonal) to within two bf16 roundings."""
+    rng = np.random.default_rng(7)
+    for g, k in ((256, 768), (64, 192), (16, 48), (4, 8)):
+        x = oracle.f32_to_bf16(rng.standard_normal((64, k), dtype=np.float32))
+        got = oracle.rotate_groups_bf16(x, g)
+        xf = oracle.bf16_to_f32(x).astype(np.float64)
+        h = regular_hadamard(g).astype(np.float64) / np.sqrt(g)
+        ref = np.concatenate([xf[:, g0:g0 + g] @ h for g0 in range(0, k, g)], axis=1)
+        want = oracle.f32_to_bf16(ref.astype(np.float32))
+        assert np.mean(got == want) > 0.995, g
+        gf = oracle.bf16_to_f32(got).astype(np.float64)
+        assert np.all(np.abs(gf - ref) <= 2.0 ** -8 * np.abs(ref) + 1e-6 * np.abs(xf).max()), g
+        back = oracle.bf16_to_f32(oracle.rotate_groups_bf16(got, g)).astype(np.float64)
+        assert np.all(np.abs(back - xf) <= 2.0 ** -6 * np.abs(xf).max()), g
