@@ -63,6 +63,9 @@ typedef enum sc_scale_layout { SC_SCALE_TENSOR = 0, SC_SCALE_COLUMNS = 1 } sc_sc
  * TensorGEMM.linear(... c: MTLBuffer) writes fp32, TensorGEMM.swift:264-267). */
 typedef enum sc_out_type { SC_OUT_BF16 = 0, SC_OUT_F32 = 1 } sc_out_type;
 
+/* Activation element type of the W8A8 entries: bf16, or fp32 (the reference's activation). */
+typedef enum sc_in_type { SC_IN_BF16 = 0, SC_IN_F32 = 1 } sc_in_type;
+
 /* Flags of sc_weight_create. */
 #define SC_WEIGHT_VALUES_ON_DEVICE 0x1u /* values and scales are device pointers (else host) */
 #define SC_WEIGHT_PUBLISHED_NK 0x2u     /* values are the published [N, K] rows, not the map's [K, N] */
@@ -172,6 +175,25 @@ SC_API sc_status sc_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, in
  * the reference's C buffer; the same sum, scale and bias, without the final rounding to bf16). */
 SC_API sc_status sc_linear_ex(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, void* y,
                               sc_out_type y_type, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * W8A8, the forward of the int8 weight's own author (TensorGEMMInt8.swift, ComfyUI's int8_linear): the
+ * activation x [m, k] (bf16 or fp32) rotated by the weight's convrot group if it has one, quantized to
+ * int8 per row over the whole row (s_x = max(max|y| / 127, 1e-30), q_x = clamp(rint(y / s_x), -128, 127),
+ * correctly rounded divisions, half to even: W8A8.quantize, :198-221), multiplied exactly in int32 by
+ * the weight's int8 codes on the tensor cores (tcgen05 kind::i8), then y = float(acc) * (s_x * s_w)
+ * (scale_products, :155-160), + bias when given, in fp32 or rounded to bf16.  int8 weights only
+ * (SC_INVALID_ARG otherwise); K a multiple of 8, at most 32768.  The workspace
+ * (sc_w8a8_workspace_size) holds the weight's codes made signed, x's codes and s_x: 256-byte aligned.
+ */
+SC_API sc_status sc_w8a8_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* bytes);
+SC_API sc_status sc_linear_w8a8(sc_ctx* ctx, const sc_weight* w, const void* x, sc_in_type x_type, int64_t m,
+                                const sc_bf16* bias, void* y, sc_out_type y_type, void* workspace,
+                                size_t workspace_bytes, void* stream);
+/* The quantization on its own (quantize_rows, TensorGEMMInt8.swift:137-151): codes int8 rows `ld` bytes
+ * apart (ld >= k, a multiple of 16), scales fp32 [m].  group 0: no rotation. */
+SC_API sc_status sc_quantize_rows(sc_ctx* ctx, const void* x, sc_in_type x_type, int64_t m, int64_t k, int group,
+                                  int8_t* codes, int64_t ld, float* scales, void* stream);
 
 /* Operation fused into the epilogue of sc_linear_epilogue, applied to v = acc * s[n] + bias[n] (fp32). */
 typedef enum sc_epilogue {

@@ -60,6 +60,8 @@ def lib() -> ctypes.CDLL:
         L.orc_set_threads.argtypes = [I]
         L.orc_rotate_groups_bf16.argtypes = [P, I64, I64, I, P]
         L.orc_dequantize_rotated.argtypes = [P, I64, I64, I, P, P]
+        L.orc_w8a8_quantize.argtypes = [P, I64, I64, I, P, P]
+        L.orc_linear_w8a8.argtypes = [P, P, I64, I64, I64, P, P, P, P, P]
         L.orc_max_threads.restype = I
         _lib = L
     return _lib
@@ -176,3 +178,29 @@ def dequantize_rotated(q_kn: np.ndarray, group: int, s: np.ndarray) -> np.ndarra
     out = np.empty((k, n), np.float32)
     lib().orc_dequantize_rotated(_p(q), k, n, group, _p(s), _p(out))
     return out
+
+
+def w8a8_quantize(x: np.ndarray, group: int = 0):
+    """W8A8.quantize (TensorGEMMInt8.swift:198-221) per row of fp32 x [m, k]: (codes int8 [m, k], scales fp32 [m])."""
+    x = np.ascontiguousarray(x, np.float32)
+    m, k = x.shape
+    assert group == 0 or k % group == 0
+    codes = np.empty((m, k), np.int8)
+    scales = np.empty(m, np.float32)
+    lib().orc_w8a8_quantize(_p(x), m, k, group, _p(codes), _p(scales))
+    return codes, scales
+
+
+def linear_w8a8(codes: np.ndarray, sx: np.ndarray, q_kn: np.ndarray, sw: np.ndarray, bias_bf16: np.ndarray | None = None):
+    """float(codes . q) * (s_x * s_w) (+ bias): returns (c fp32 [m, n], y bf16 [m, n])."""
+    codes = np.ascontiguousarray(codes, np.int8)
+    q = np.ascontiguousarray(q_kn, np.int8)
+    m, k = codes.shape
+    n = q.shape[1]
+    sx = np.ascontiguousarray(sx, np.float32)
+    sw = np.ascontiguousarray(np.broadcast_to(np.asarray(sw, np.float32), (n,)), np.float32)
+    b = None if bias_bf16 is None else np.ascontiguousarray(bias_bf16, np.uint16)
+    c = np.empty((m, n), np.float32)
+    y = np.empty((m, n), np.uint16)
+    lib().orc_linear_w8a8(_p(codes), _p(sx), m, k, n, _p(q), _p(sw), _p(b), _p(c), _p(y))
+    return c, y

@@ -262,6 +262,53 @@ void orc_dequantize_rotated(const int8_t* q, int64_t k, int64_t n, int group, co
     }
 }
 
+void orc_w8a8_quantize(const float* x, int64_t m, int64_t k, int group, int8_t* codes, float* scales) {
+    const float norm = group > 0 ? rotation_norm(group) : 1.0f;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < m; ++r) {
+        float* y = (float*)malloc((size_t)k * sizeof(float));
+        for (int64_t i = 0; i < k; ++i) y[i] = x[r * k + i];
+        if (group > 0) {
+            for (int64_t g0 = 0; g0 < k; g0 += group) {
+                rotate_group_f32(y + g0, group);
+                for (int i = 0; i < group; ++i) y[g0 + i] = y[g0 + i] * norm;
+            }
+        }
+        float top = 0.0f;
+        for (int64_t i = 0; i < k; ++i) top = fabsf(y[i]) > top ? fabsf(y[i]) : top;
+        float scale = top / 127.0f;
+        if (!(scale >= 1e-30f)) scale = 1e-30f;
+        scales[r] = scale;
+        for (int64_t i = 0; i < k; ++i) {
+            float q = rintf(y[i] / scale);          /* default rounding mode: half to even */
+            q = q < -128.0f ? -128.0f : (q > 127.0f ? 127.0f : q);
+            codes[r * k + i] = (int8_t)q;
+        }
+        free(y);
+    }
+}
+
+void orc_linear_w8a8(const int8_t* codes, const float* sx, int64_t m, int64_t k, int64_t n, const int8_t* q,
+                     const float* sw, const uint16_t* bias, float* c, uint16_t* y) {
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < m; ++r) {
+        int64_t* acc = (int64_t*)calloc((size_t)n, sizeof(int64_t));
+        for (int64_t i = 0; i < k; ++i) {
+            const int64_t a = codes[r * k + i];
+            if (a == 0) continue;
+            const int8_t* qr = q + i * n;
+            for (int64_t j = 0; j < n; ++j) acc[j] += a * qr[j];
+        }
+        for (int64_t j = 0; j < n; ++j) {
+            float v = (float)(int32_t)acc[j] * (sx[r] * sw[j]);
+            if (bias) v = v + orc_bf16_to_f32(bias[j]);
+            c[r * n + j] = v;
+            if (y) y[r * n + j] = orc_f32_to_bf16(v);
+        }
+        free(acc);
+    }
+}
+
 void orc_set_threads(int threads) {
 #ifdef _OPENMP
     if (threads > 0) omp_set_num_threads(threads);

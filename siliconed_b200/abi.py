@@ -27,6 +27,7 @@ SCALE_TENSOR, SCALE_COLUMNS = 0, 1
 VALUES_ON_DEVICE, PUBLISHED_NK = 0x1, 0x2
 OUT_BF16, OUT_F32 = 0, 1
 EPI_GELU_TANH, EPI_GATED_RESIDUAL = 1, 2
+IN_BF16, IN_F32 = 0, 1
 
 _P, _I64, _I, _U32, _SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint32, ctypes.c_size_t
 _PP = ctypes.POINTER(ctypes.c_void_p)
@@ -48,6 +49,9 @@ SIGNATURES = {
     "sc_linear_ex": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _SZ, _P]),
     "sc_linear_epilogue": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _P, _SZ, _P]),
     "sc_weight_set_rotation": (_I, [_P, _P, _I]),
+    "sc_w8a8_workspace_size": (_I, [_P, _P, _I64, ctypes.POINTER(_SZ)]),
+    "sc_linear_w8a8": (_I, [_P, _P, _P, _I, _I64, _P, _P, _I, _P, _SZ, _P]),
+    "sc_quantize_rows": (_I, [_P, _P, _I, _I64, _I64, _I, _P, _I64, _P, _P]),
     "sc_rotate_activation": (_I, [_P, _P, _I64, _I64, _I, _P, _P]),
     "sc_linear_ex_noalloc": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P]),
     "sc_linear_allgather": (_I, [_P, _P, _P, _I64, _P, _P, _P, _I, _I, _I64, _I64, ctypes.c_uint32, _P, _SZ, _P]),

@@ -23,7 +23,7 @@ DIT_CSRC = os.path.join(CSRC, "dit")
 DIT_SOURCES = ["sd_kernels.cu"]
 
 SOURCES = ["sc_abi.cu", "sc_weight.cu", "sc_gemm.cu", "sc_gemm_pair.cu", "sc_gemm_bf16.cu", "sc_gemm_skinny.cu",
-           "sc_gemv.cu", "sc_no_alloc.cu", "sc_rotate.cu"]
+           "sc_gemv.cu", "sc_no_alloc.cu", "sc_rotate.cu", "sc_w8a8.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

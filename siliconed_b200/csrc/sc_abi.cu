@@ -114,6 +114,27 @@ sc_status make_tmap_widened(sc_ctx* ctx, const sc_weight* w, void* widened, CUte
   return SC_OK;
 }
 
+// Map over 8-bit codes [rows][inner] with rows `stride` bytes apart: box 128 x 128, 128-byte swizzle
+// (the int8 GEMM's operands: 128 codes of K per stage row).
+sc_status make_tmap_codes(sc_ctx* ctx, const void* base, int64_t inner, int64_t rows, int64_t stride, CUtensorMap* map) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride)};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, SC_CUDA_ERROR, "cuTensorMapEncodeTiled (codes) failed: " + std::to_string(r));
+  return SC_OK;
+}
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+int64_t w8a8_ld(int64_t k) { return (k + 15) / 16 * 16; }
+size_t w8a8_workspace(const sc_weight* w, int64_t m) {
+  return align256(signed_codes_bytes(w)) + align256(static_cast<size_t>(m * w8a8_ld(w->k))) +
+         align256(static_cast<size_t>(m) * 4);
+}
+
 sc_status make_tmap_w(sc_ctx* ctx, sc_weight* w) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w->k_pad), static_cast<cuuint64_t>(w->n_pad)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w->k_pad)};
@@ -437,6 +458,75 @@ sc_status sc_dequantize(sc_ctx* ctx, const sc_weight* w, float* out, void* strea
     return check_cuda(ctx, launch_dequantize_rotated(w, out, static_cast<cudaStream_t>(stream)),
                       "rotated dequantize launch");
   return check_cuda(ctx, launch_dequantize(w, out, static_cast<cudaStream_t>(stream)), "dequantize launch");
+}
+
+sc_status sc_w8a8_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* bytes) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (w == nullptr || bytes == nullptr || m < 0) return fail(ctx, SC_INVALID_ARG, "bad argument");
+  *bytes = m == 0 ? 0 : w8a8_workspace(w, m);
+  return SC_OK;
+}
+
+sc_status sc_quantize_rows(sc_ctx* ctx, const void* x, sc_in_type x_type, int64_t m, int64_t k, int group,
+                           int8_t* codes, int64_t ld, float* scales, void* stream) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (x_type != SC_IN_BF16 && x_type != SC_IN_F32) return fail(ctx, SC_INVALID_ARG, "unknown input type");
+  if (m < 0 || k <= 0) return fail(ctx, SC_INVALID_ARG, "m < 0 or k <= 0");
+  if (group != 0 && (!is_rotation_group(group) || k % group != 0))
+    return fail(ctx, SC_UNSUPPORTED_SHAPE, "group must be 0 or a power of 4 from 4 to 256 dividing K");
+  if (k % 8 != 0 || k > kW8A8MaxK) return fail(ctx, SC_UNSUPPORTED_SHAPE, "K must be a multiple of 8, at most 32768");
+  if (ld < k || ld % 16 != 0) return fail(ctx, SC_INVALID_ARG, "ld must be at least K and a multiple of 16");
+  if (m == 0) return SC_OK;
+  if (x == nullptr || codes == nullptr || scales == nullptr) return fail(ctx, SC_INVALID_ARG, "null argument");
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(codes)) & 15u) ||
+      (reinterpret_cast<uintptr_t>(scales) & 3u))
+    return fail(ctx, SC_UNALIGNED, "x and codes must be 16-byte aligned, scales 4-byte aligned");
+  if (!is_device_pointer(x) || !is_device_pointer(codes) || !is_device_pointer(scales))
+    return fail(ctx, SC_INVALID_ARG, "x, codes and scales must be device memory");
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  return check_cuda(ctx, launch_quantize_rows(x, x_type == SC_IN_F32, m, k, group, codes, ld, scales,
+                                              static_cast<cudaStream_t>(stream)),
+                    "quantize launch");
+}
+
+sc_status sc_linear_w8a8(sc_ctx* ctx, const sc_weight* w, const void* x, sc_in_type x_type, int64_t m,
+                         const sc_bf16* bias, void* y, sc_out_type y_type, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (w == nullptr) return fail(ctx, SC_INVALID_ARG, "null weight");
+  if (w->kind != SC_WEIGHT_INT8) return fail(ctx, SC_INVALID_ARG, "W8A8 reads int8 weights only");
+  if (x_type != SC_IN_BF16 && x_type != SC_IN_F32) return fail(ctx, SC_INVALID_ARG, "unknown input type");
+  if (y_type != SC_OUT_BF16 && y_type != SC_OUT_F32) return fail(ctx, SC_INVALID_ARG, "unknown output type");
+  if (m < 0) return fail(ctx, SC_INVALID_ARG, "m < 0");
+  if (m == 0) return SC_OK;
+  if (x == nullptr || y == nullptr) return fail(ctx, SC_INVALID_ARG, "null x or y");
+  if (m > 0x7FFFFFFF) return fail(ctx, SC_UNSUPPORTED_SHAPE, "m beyond 2^31 - 1");
+  if (w->k % 8 != 0 || w->k > kW8A8MaxK) return fail(ctx, SC_UNSUPPORTED_SHAPE, "K must be a multiple of 8, at most 32768");
+  if (w->device != ctx->device) return fail(ctx, SC_INVALID_ARG, "weight registered on another device");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u)
+    return fail(ctx, SC_UNALIGNED, "x and y must be 16-byte aligned");
+  if (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 1u)) return fail(ctx, SC_UNALIGNED, "bias must be 2-byte aligned");
+  if (!is_device_pointer(x) || !is_device_pointer(y) || (bias != nullptr && !is_device_pointer(bias)))
+    return fail(ctx, SC_INVALID_ARG, "x, y and bias must be device (or managed) memory");
+  if (workspace == nullptr || workspace_bytes < w8a8_workspace(w, m) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(ctx, SC_WORKSPACE_TOO_SMALL, "W8A8 needs a 256-byte aligned workspace of sc_w8a8_workspace_size bytes");
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* wsigned = static_cast<uint8_t*>(workspace);
+  const int64_t ld = w8a8_ld(w->k);
+  int8_t* codes = reinterpret_cast<int8_t*>(wsigned + align256(signed_codes_bytes(w)));
+  float* sx = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(codes) + align256(static_cast<size_t>(m * ld)));
+  if ((s = check_cuda(ctx, launch_sign_codes(w, wsigned, st), "sign launch")) != SC_OK) return s;
+  if ((s = check_cuda(ctx, launch_quantize_rows(x, x_type == SC_IN_F32, m, w->k, w->rotation, codes, ld, sx, st),
+                      "quantize launch")) != SC_OK)
+    return s;
+  CUtensorMap tmx, tmw;
+  if ((s = make_tmap_codes(ctx, codes, w->k, m, ld, &tmx)) != SC_OK) return s;
+  if ((s = make_tmap_codes(ctx, wsigned, w->k_pad, w->n_pad, w->k_pad, &tmw)) != SC_OK) return s;
+  return check_cuda(ctx, launch_gemm_i8(tmx, tmw, w, bias, y, y_type == SC_OUT_F32, sx, m, ctx->d_err, ctx->sm_count, st),
+                    "int8 gemm launch");
 }
 
 sc_status sc_weight_set_rotation(sc_ctx* ctx, sc_weight* w, int group) {

@@ -74,14 +74,32 @@ __device__ __forceinline__ float gelu_tanh(float v) {
   return __fdividef(v, 1.0f + e);
 }
 
-template <bool kF32Out, bool kPeers, int kOp>
+// The value of one accumulator element before the epilogue's operation.  bf16 operands: acc * s + b,
+// two roundings.  kI8 (W8A8, the int8 x int8 product of TensorGEMMInt8.swift): float(acc) * (s_x * s_w),
+// the scales' product first (scale_products, :155-160), then + bias only when there is one (a
+// missing bias adds nothing, not +0, which would turn -0 into +0).
+template <bool kI8>
+__device__ __forceinline__ float epi_value(uint32_t raw, float sc, float bi, float sxr, bool has_bias) {
+  if (kI8) {
+    const float v = __fmul_rn(__int2float_rn(static_cast<int>(raw)), __fmul_rn(sxr, sc));
+    return has_bias ? __fadd_rn(v, bi) : v;
+  }
+  return __fadd_rn(__fmul_rn(__uint_as_float(raw), sc), bi);
+}
+
+// kI8: both operands int8 codes (x's per-row codes, the weight's codes made signed), 128 codes = 128
+// bytes per K stage, tcgen05.mma kind::i8 into s32 accumulators; row_scales holds s_x per row.
+template <bool kF32Out, bool kPeers, int kOp, bool kI8>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const float* __restrict__ scales, const uint16_t* __restrict__ bias, void* __restrict__ y_out,
                    int M, int N, int k_tiles, int m_tiles, int n_tiles, int* err,
-                   const __grid_constant__ PeerOut peers, const float* __restrict__ gate) {
+                   const __grid_constant__ PeerOut peers, const float* __restrict__ gate,
+                   const float* __restrict__ row_scales) {
   static_assert(kOp != kOpResidual || kF32Out, "the residual is fp32");
   static_assert(kOp != kOpGelu || !kF32Out, "the GELU output is bf16");
+  static_assert(!kI8 || (kOp == kOpNone && !kPeers), "W8A8 stores plain outputs");
+  constexpr int kBKElems = kI8 ? 128 : BK;  // K elements per 128-byte stage row
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -130,8 +148,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort, err, kSiteProducerEmpty)) break;
           if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (kABytes + kBBytes));
           const uint32_t bar = peer_addr(&s.full[stage], 0);
-          tma_load_2d_pair(s.a[stage], &tm_x, bar, kt * BK, row0);
-          tma_load_2d_pair(s.b[stage], &tm_w, bar, kt * BK, col0);
+          tma_load_2d_pair(s.a[stage], &tm_x, bar, kt * kBKElems, row0);
+          tma_load_2d_pair(s.b[stage], &tm_w, bar, kt * kBKElems, col0);
           issued |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == kStages) {
@@ -149,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA) ----------------
     if (leader && lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16(2 * BM, BN);
+      const uint32_t idesc = kI8 ? umma_idesc_s8(2 * BM, BN) : umma_idesc_bf16(2 * BM, BN);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
@@ -173,8 +191,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a0 = smem_u32(s.a[cur]), b0 = smem_u32(s.b[cur]);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            tc_mma_f16_pair(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
-                            (kt | kk) != 0 ? 1u : 0u);
+            if (kI8)
+              tc_mma_i8_pair(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
+                             (kt | kk) != 0 ? 1u : 0u);
+            else
+              tc_mma_f16_pair(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
+                              (kt | kk) != 0 ? 1u : 0u);
           tc_commit_pair_both(&s.empty[cur], 0x3);
         }
         if (!ok) break;
@@ -193,11 +215,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool vec_ok = (N % 8) == 0, vec4_ok = (N % 4) == 0;
+    const bool has_bias = bias != nullptr;
     for (int tile = pair; tile < num_tiles; tile += pairs) {
       int mt, nt;
       tile_coords(tile, m_tiles, n_tiles, mt, nt);
       const int n0 = nt * BN;
       const int row = mt * 2 * BM + static_cast<int>(rank) * BM + ew * 32 + lane;
+      const float sxr = kI8 && row < M ? row_scales[row] : 0.0f;
       __syncwarp();
       for (int c = lane; c < BN; c += 32) {
         const int n = n0 + c;
@@ -250,8 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kF32Out) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            r[j] = __float_as_uint(
-                __fadd_rn(__fmul_rn(__uint_as_float(r[j]), s_scale[ch * 32 + j]), s_bias[ch * 32 + j]));
+            r[j] = __float_as_uint(epi_value<kI8>(r[j], s_scale[ch * 32 + j], s_bias[ch * 32 + j], sxr, has_bias));
           const bool staged = kOp == kOpResidual ? res_fast : vec4_ok;
           if (staged) {
             // 32 rows x 32 fp32: row `lane`'s 16-byte unit q at st[lane * 8 + (q ^ (lane & 7))]
@@ -303,9 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            float v0 = __fadd_rn(__fmul_rn(__uint_as_float(r[j]), s_scale[ch * 32 + j]), s_bias[ch * 32 + j]);
-            float v1 = __fadd_rn(__fmul_rn(__uint_as_float(r[j + 1]), s_scale[ch * 32 + j + 1]),
-                                 s_bias[ch * 32 + j + 1]);
+            float v0 = epi_value<kI8>(r[j], s_scale[ch * 32 + j], s_bias[ch * 32 + j], sxr, has_bias);
+            float v1 = epi_value<kI8>(r[j + 1], s_scale[ch * 32 + j + 1], s_bias[ch * 32 + j + 1], sxr, has_bias);
             if (kOp == kOpGelu) {
               v0 = gelu_tanh(v0);
               v1 = gelu_tanh(v1);
@@ -418,11 +440,11 @@ __global__ void __launch_bounds__(256) widen_codes(const uint4* __restrict__ cod
   }
 }
 
-template <bool kF32Out, bool kPeers, int kOp = kOpNone>
+template <bool kF32Out, bool kPeers, int kOp = kOpNone, bool kI8 = false>
 cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const sc_weight* w, const uint16_t* bias,
                         void* y, int64_t m, int* err, int sm_count, cudaStream_t stream, const PeerOut& peers,
-                        const float* gate = nullptr) {
-  auto kernel = gemm_bf16_pair<kF32Out, kPeers, kOp>;
+                        const float* gate = nullptr, const float* row_scales = nullptr) {
+  auto kernel = gemm_bf16_pair<kF32Out, kPeers, kOp, kI8>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e =
@@ -432,7 +454,9 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   }
   const int m_tiles = static_cast<int>((m + 2 * BM - 1) / (2 * BM));
   const int n_tiles = static_cast<int>(w->n_pad / BN);
-  const int k_tiles = static_cast<int>(w->k_pad / BK);
+  // kI8: 128 codes per stage; the weight's K padding is a multiple of 64, and a last stage past it
+  // reads zeros (the copy's fill), as x's codes are zero past K.
+  const int k_tiles = static_cast<int>(kI8 ? (w->k_pad + 127) / 128 : w->k_pad / BK);
   const int tiles = m_tiles * n_tiles;
   const int max_pairs = sm_count / 2;
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
@@ -449,7 +473,26 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias, y,
-                            static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers, gate);
+                            static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers, gate,
+                            row_scales);
+}
+
+// The weight's arena codes (int8 stored biased by 128) made signed again for the int8 MMA: code ^ 0x80.
+__global__ void __launch_bounds__(256) sign_codes(const uint4* __restrict__ codes, uint4* __restrict__ out,
+                                                  int64_t chunks) {
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * (256 * kWidenPer) + threadIdx.x;
+  uint4 in[kWidenPer];
+#pragma unroll
+  for (int u = 0; u < kWidenPer; ++u) {
+    const int64_t i = base + u * 256;
+    in[u] = i < chunks ? __ldcs(codes + i) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int u = 0; u < kWidenPer; ++u) {
+    const int64_t i = base + u * 256;
+    if (i < chunks)
+      out[i] = make_uint4(in[u].x ^ 0x80808080u, in[u].y ^ 0x80808080u, in[u].z ^ 0x80808080u, in[u].w ^ 0x80808080u);
+  }
 }
 
 // One rank waits until every rank's flag for it reached `epoch` (epochs only grow), bounded.
@@ -513,6 +556,31 @@ cudaError_t launch_gemm_bf16_op(const CUtensorMap& tmap_x, const CUtensorMap& tm
     return gemm_bf16::launch_gemm<true, false, gemm_bf16::kOpResidual>(tmap_x, tmap_w, w, bias, y, m, err, sm_count,
                                                                        stream, none, gate);
   return cudaErrorInvalidValue;
+}
+
+size_t signed_codes_bytes(const sc_weight* w) {
+  return static_cast<size_t>(w->n_pad) * static_cast<size_t>(w->k_pad);
+}
+
+cudaError_t launch_sign_codes(const sc_weight* w, void* out, cudaStream_t stream) {
+  const int64_t chunks = w->n_pad * w->k_pad / 16;
+  const int64_t per_block = 256LL * gemm_bf16::kWidenPer;
+  const int64_t blocks64 = (chunks + per_block - 1) / per_block;
+  if (blocks64 > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  gemm_bf16::sign_codes<<<static_cast<int>(blocks64 > 0 ? blocks64 : 1), 256, 0, stream>>>(
+      reinterpret_cast<const uint4*>(w->values), static_cast<uint4*>(out), chunks);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_i8(const CUtensorMap& tmap_codes, const CUtensorMap& tmap_w, const sc_weight* w,
+                           const uint16_t* bias, void* y, bool f32_out, const float* row_scales, int64_t m, int* err,
+                           int sm_count, cudaStream_t stream) {
+  const PeerOut none = {};
+  using namespace gemm_bf16;
+  return f32_out ? launch_gemm<true, false, kOpNone, true>(tmap_codes, tmap_w, w, bias, y, m, err, sm_count, stream,
+                                                           none, nullptr, row_scales)
+                 : launch_gemm<false, false, kOpNone, true>(tmap_codes, tmap_w, w, bias, y, m, err, sm_count, stream,
+                                                            none, nullptr, row_scales);
 }
 
 cudaError_t launch_gather_wait(const uint32_t* flags, int world, uint32_t epoch, int* err, cudaStream_t stream) {

@@ -105,6 +105,16 @@ cudaError_t launch_gemm_bf16_peers(const CUtensorMap& tmap_x, const CUtensorMap&
                                    const uint16_t* bias, const PeerOut& peers, int64_t m, int* err, int sm_count,
                                    cudaStream_t stream);
 cudaError_t launch_gather_wait(const uint32_t* flags, int world, uint32_t epoch, int* err, cudaStream_t stream);
+// W8A8 (sc_w8a8.cu, sc_gemm_bf16.cu): the weight's codes made signed [n_pad][k_pad] in the workspace;
+// x rotated (group > 0) and quantized per row into codes [m][ld] and s_x [m]; the int8 x int8 pair GEMM.
+size_t signed_codes_bytes(const sc_weight* w);
+cudaError_t launch_sign_codes(const sc_weight* w, void* out, cudaStream_t stream);
+cudaError_t launch_quantize_rows(const void* x, bool x_f32, int64_t m, int64_t k, int group, int8_t* codes, int64_t ld,
+                                 float* scales, cudaStream_t stream);
+cudaError_t launch_gemm_i8(const CUtensorMap& tmap_codes, const CUtensorMap& tmap_w, const sc_weight* w,
+                           const uint16_t* bias, void* y, bool f32_out, const float* row_scales, int64_t m, int* err,
+                           int sm_count, cudaStream_t stream);
+constexpr int64_t kW8A8MaxK = 32768;  // a row held whole in shared memory as fp32 (128 KB)
 // The bf16-operand pair GEMM with a fused epilogue operation: op 1 = GELU (tanh) before the bf16 store,
 // op 2 = y (fp32) += gate[n] * v in place (the gated residual).
 cudaError_t launch_gemm_bf16_op(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,

@@ -236,6 +236,29 @@ class QuantizedWeight:
                                                        _ptr(gate), _ptr(workspace), ws_bytes, _stream_ptr(stream)))
         return out
 
+    def w8a8_workspace_bytes(self, m: int) -> int:
+        b = ctypes.c_size_t()
+        self.ctx.check(self.ctx.lib.sc_w8a8_workspace_size(self.ctx.ptr, self.ptr, int(m), ctypes.byref(b)))
+        return int(b.value)
+
+    def linear_w8a8(self, x, out, bias=None, workspace=None, stream=None):
+        """sc_linear_w8a8: x (bf16 or fp32 [M, K]) rotated if the weight is convrot, quantized to int8 per
+        row, times the int8 codes exactly, then float(acc) * (s_x * s_w) (+ bias) into `out` (bf16 or fp32)."""
+        if x.dtype not in (torch.bfloat16, torch.float32) or not x.is_cuda or x.dim() != 2 or x.shape[1] != self.k:
+            raise SiliconedError(abi.INVALID_ARG, f"x must be a CUDA bf16 or fp32 [M, {self.k}] tensor")
+        x = x.contiguous()
+        m = x.shape[0]
+        if out.dtype not in (torch.bfloat16, torch.float32) or tuple(out.shape) != (m, self.n) or not out.is_contiguous():
+            raise SiliconedError(abi.INVALID_ARG, f"out must be a contiguous bf16 or fp32 [{m}, {self.n}] tensor")
+        if workspace is None:
+            workspace = self.ctx.workspace(self.w8a8_workspace_bytes(m), x.device)
+        ws_bytes = workspace.numel() * workspace.element_size()
+        self.ctx.check(self.ctx.lib.sc_linear_w8a8(
+            self.ctx.ptr, self.ptr, _ptr(x), abi.IN_F32 if x.dtype == torch.float32 else abi.IN_BF16, m, _ptr(bias),
+            _ptr(out), abi.OUT_F32 if out.dtype == torch.float32 else abi.OUT_BF16, _ptr(workspace), ws_bytes,
+            _stream_ptr(stream)))
+        return out
+
     def linear(self, x, bias=None, out=None, workspace=None, stream=None):
         """y = bf16((x . q) * s + bias), dispatching on M (GEMV for M <= 32, tensor-core GEMM above)."""
         return self._product("sc_linear", x, bias, out, workspace, stream)
@@ -253,6 +276,19 @@ def rotate_activation(ctx: Context, x, group: int, out=None, stream=None):
     ctx.check(ctx.lib.sc_rotate_activation(ctx.ptr, _ptr(x), x.shape[0], x.shape[1], int(group), _ptr(out),
                                            _stream_ptr(stream)))
     return out
+
+
+def quantize_rows(ctx: Context, x, group: int = 0, stream=None):
+    """sc_quantize_rows: (codes int8 [M, K], s_x fp32 [M]) of x (bf16 or fp32 [M, K]), rotated by `group` first."""
+    if x.dtype not in (torch.bfloat16, torch.float32) or not x.is_cuda or x.dim() != 2 or not x.is_contiguous():
+        raise SiliconedError(abi.INVALID_ARG, "x must be a contiguous CUDA bf16 or fp32 [M, K] tensor")
+    m, k = x.shape
+    ld = (k + 15) // 16 * 16
+    codes = torch.empty((m, ld), dtype=torch.int8, device=x.device)
+    scales = torch.empty(m, dtype=torch.float32, device=x.device)
+    ctx.check(ctx.lib.sc_quantize_rows(ctx.ptr, _ptr(x), abi.IN_F32 if x.dtype == torch.float32 else abi.IN_BF16, m, k,
+                                       int(group), _ptr(codes), ld, _ptr(scales), _stream_ptr(stream)))
+    return codes[:, :k], scales
 
 
 class WeightProducts:

@@ -203,3 +203,56 @@ def test_rotate_groups_is_the_orthogonal_rotation():
         assert np.all(np.abs(gf - ref) <= 2.0 ** -8 * np.abs(ref) + 1e-6 * np.abs(xf).max()), g
         back = oracle.bf16_to_f32(oracle.rotate_groups_bf16(got, g)).astype(np.float64)
         assert np.all(np.abs(back - xf) <= 2.0 ** -6 * np.abs(xf).max()), g
+
+
+# ---------------------------------------------------------------------------------------------
+# W8A8 (TensorGEMMInt8.swift): the oracle against an independent numpy restatement of the recipe
+
+
+def numpy_w8a8_quantize(x: np.ndarray, group: int):
+    """W8A8.quantize restated on whole columns of rows at once in numpy fp32 (IEEE adds, an IEEE
+    division, np.rint half to even)."""
+    y = x.astype(np.float32).copy()
+    if group:
+        norm = np.float32(1.0 / np.sqrt(group))
+        m, k = y.shape
+        v = y.reshape(m, k // group, group)
+        span = 1
+        while span < group:
+            w = v.reshape(m, k // group, group // (4 * span), 4, span)
+            a, b, c, d = w[:, :, :, 0].copy(), w[:, :, :, 1].copy(), w[:, :, :, 2].copy(), w[:, :, :, 3].copy()
+            p, mm, u, ww = a + b, a - b, c + d, c - d
+            w[:, :, :, 0], w[:, :, :, 1], w[:, :, :, 2], w[:, :, :, 3] = p + ww, p - ww, mm + u, u - mm
+            span *= 4
+        y = v.reshape(m, k) * norm
+    top = np.abs(y).max(axis=1)
+    scale = np.maximum(top / np.float32(127), np.float32(1e-30)).astype(np.float32)
+    codes = np.clip(np.rint(y / scale[:, None]), -128, 127).astype(np.int8)
+    return codes, scale
+
+
+@pytest.mark.parametrize("m,k,group", [(150, 768, 256), (70, 10240, 256), (65, 448, 64), (33, 520, 0), (9, 16, 4)])
+def test_w8a8_is_the_recipe(m, k, group):
+    """The cases of W8A8KernelTests.swift:71-78 (rows of values in +-3, a row of zeros whose scale is the
+    recipe's floor 1e-30, a massive column); codes, scales and the product at the bit."""
+    rng = np.random.default_rng(m * k + group)
+    a = ((rng.random((m, k), dtype=np.float32) - 0.5) * 6).astype(np.float32)
+    a[3 % m] = 0
+    a[:, k // 3] *= 300
+    codes, sx = oracle.w8a8_quantize(a, group)
+    ref_codes, ref_sx = numpy_w8a8_quantize(a, group)
+    assert np.array_equal(sx.view(np.uint32), ref_sx.view(np.uint32))
+    assert np.array_equal(codes, ref_codes)
+    assert sx[3 % m] == np.float32(1e-30) and not codes[3 % m].any()
+    n = 40
+    q = rng.integers(-127, 128, (k, n), dtype=np.int16).astype(np.int8)
+    sw = ((np.abs(rng.random(n, dtype=np.float32) - 0.5) + 0.01) / 64).astype(np.float32)
+    c, _ = oracle.linear_w8a8(codes, sx, q, sw)
+    acc = codes.astype(np.int64) @ q.astype(np.int64)
+    assert np.abs(acc).max() < 2 ** 31
+    want = acc.astype(np.int32).astype(np.float32) * (sx[:, None] * sw[None, :])
+    assert np.array_equal(c.view(np.uint32), want.view(np.uint32))
+    b = oracle.f32_to_bf16(rng.standard_normal(n, dtype=np.float32))
+    cb, yb = oracle.linear_w8a8(codes, sx, q, sw, b)
+    assert np.array_equal(cb.view(np.uint32), (want + oracle.bf16_to_f32(b)).view(np.uint32))
+    assert np.array_equal(yb, oracle.f32_to_bf16(cb))
