@@ -213,6 +213,23 @@ SC_API sc_status sc_linear_epilogue(sc_ctx* ctx, const sc_weight* w, const sc_bf
                                     void* y, sc_epilogue op, const float* gate, void* workspace, size_t workspace_bytes,
                                     void* stream);
 
+/*
+ * sc_linear_ex from and to host memory: y_host = x_host . W (+ bias), with the copies overlapped with the
+ * products.  The rows go in chunks of whole 256-row tiles (chunk_rows, 0 for the library's choice: about
+ * m / 4, at least 512 rows, at most 32 chunks); chunk c's copy in (x_host -> x_dev), product (into y_dev)
+ * and copy out (y_dev -> y_host) run on the context's two copy streams and on `stream`, so that one
+ * chunk's product runs while the next chunk arrives and the last leaves.  Every chunk of a split batch
+ * runs the pair GEMM, so each row has the bits the whole batch would give it on the device.  x_dev
+ * [m, k] bf16 and y_dev [m, n] are the caller's device buffers (the library allocates nothing); the
+ * workspace is sc_workspace_size's for the largest chunk (that of m suffices).  Asynchronous on
+ * `stream`: y_host is complete when `stream` reaches the call's end; x_host and y_host must be page-locked
+ * for the copies to overlap.  No counterpart in the reference, where the GPU reads the host's memory
+ * (Apple silicon's unified memory: the MTLBuffers of WeightProducts.linear are wrapped no-copy).
+ */
+SC_API sc_status sc_linear_host(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x_host, int64_t m, const sc_bf16* bias,
+                                void* y_host, sc_out_type y_type, sc_bf16* x_dev, void* y_dev, void* workspace,
+                                size_t workspace_bytes, int64_t chunk_rows, void* stream);
+
 /* sc_linear_ex with its scratch in a 32 MiB device array of the library instead of a workspace: it
  * allocates nothing and takes no workspace argument.  No counterpart in the reference: it serves
  * callers that have no scratch buffer to pass (a binding that keeps the signature of

@@ -33,6 +33,9 @@ struct sc_ctx {
                          // fused gather's CTA counter (zero between launches)
   sc_encode_tiled_fn encode_tiled = nullptr;
   std::string last_error;
+  // sc_linear_host's copy streams and events, created on its first call and kept with the context.
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  cudaEvent_t host_events[2 * 32 + 2] = {};
 };
 
 struct sc_weight {

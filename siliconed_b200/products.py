@@ -236,6 +236,32 @@ class QuantizedWeight:
                                                        _ptr(gate), _ptr(workspace), ws_bytes, _stream_ptr(stream)))
         return out
 
+    def linear_host(self, x_host, out_host, bias=None, x_dev=None, y_dev=None, workspace=None, chunk_rows: int = 0,
+                    stream=None):
+        """sc_linear_host: out_host (CPU, bf16 or fp32 [M, N]) = x_host (CPU bf16 [M, K]) . W + bias, the copies
+        overlapped with the products in chunks of rows.  Pinned host tensors let the copies overlap; x_dev /
+        y_dev are device staging buffers (allocated here when not given)."""
+        if x_host.dtype != torch.bfloat16 or x_host.is_cuda or x_host.dim() != 2 or x_host.shape[1] != self.k:
+            raise SiliconedError(abi.INVALID_ARG, f"x_host must be a CPU bf16 [M, {self.k}] tensor")
+        m = x_host.shape[0]
+        if out_host.dtype not in (torch.bfloat16, torch.float32) or out_host.is_cuda or \
+                tuple(out_host.shape) != (m, self.n) or not out_host.is_contiguous() or not x_host.is_contiguous():
+            raise SiliconedError(abi.INVALID_ARG, f"out_host must be a contiguous CPU bf16 or fp32 [{m}, {self.n}] tensor")
+        dev = f"cuda:{self.ctx.device}"
+        if x_dev is None:
+            x_dev = torch.empty((m, self.k), dtype=torch.bfloat16, device=dev)
+        if y_dev is None:
+            y_dev = torch.empty((m, self.n), dtype=out_host.dtype, device=dev)
+        need = self.workspace_bytes(m)
+        if need and workspace is None:
+            workspace = self.ctx.workspace(need, dev)
+        ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        y_type = abi.OUT_F32 if out_host.dtype == torch.float32 else abi.OUT_BF16
+        self.ctx.check(self.ctx.lib.sc_linear_host(self.ctx.ptr, self.ptr, _ptr(x_host), m, _ptr(bias), _ptr(out_host),
+                                                   y_type, _ptr(x_dev), _ptr(y_dev), _ptr(workspace), ws_bytes,
+                                                   int(chunk_rows), _stream_ptr(stream)))
+        return out_host
+
     def w8a8_workspace_bytes(self, m: int) -> int:
         b = ctypes.c_size_t()
         self.ctx.check(self.ctx.lib.sc_w8a8_workspace_size(self.ctx.ptr, self.ptr, int(m), ctypes.byref(b)))

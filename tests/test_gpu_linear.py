@@ -578,3 +578,32 @@ def test_fused_epilogue_guards(ctx):
     ctx.check(linear_epilogue(ctx, w, x256, 256, None, r, abi.EPI_GATED_RESIDUAL, gate))
     ctx.poll_errors()
     w.close()
+
+
+# ---------------------------------------------------------------------------------------------
+# sc_linear_host: host buffers, copies overlapped with the products in chunks of rows
+
+
+@pytest.mark.parametrize("m,chunk", [(4096, 0), (4096, 1024), (1000, 0), (700, 512), (600, 0), (3, 0), (40, 0),
+                                     (2000, 256)])
+def test_linear_host_has_the_device_bits(ctx, m, chunk):
+    """Chunked copies and products give each row the bits of the whole batch's device product."""
+    g = np.random.default_rng(m + chunk)
+    k, n = 768, 1280
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+    s = (np.abs(g.standard_normal(n)) * 1e-3 + 1e-6).astype(np.float32)
+    w = QuantizedWeight(ctx, q, abi.WEIGHT_INT8, s)
+    bd = bf16_dev(configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.01))
+    x_host = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory()
+    for f32 in (False, True):
+        want = linear_ex(ctx, w, bf16_dev(x), m, bd, f32, workspace=True)
+        out = torch.empty((m, n), dtype=torch.float32 if f32 else torch.bfloat16).pin_memory()
+        out.fill_(float("nan"))
+        w.linear_host(x_host, out, bias=bd, chunk_rows=chunk)
+        torch.cuda.synchronize()
+        ctx.poll_errors()
+        a = want.cpu().view(torch.int32 if f32 else torch.int16).numpy()
+        b = out.view(torch.int32 if f32 else torch.int16).numpy()
+        assert np.array_equal(a, b), f"m {m}, chunk {chunk}, f32 {f32}: {int(np.sum(a != b))} differ"
+    w.close()
