@@ -60,7 +60,9 @@ def test_quantize_rows_is_the_recipe(ctx, m, k, group, bf16_in):
 @pytest.mark.parametrize("m,k,n,group,per_column", [(150, 768, 96, 256, True), (70, 10240, 72, 256, True),
                                                     (65, 448, 130, 64, False), (33, 520, 40, 0, True),
                                                     (600, 3072, 1000, 0, True), (1024, 3072, 3072, 256, True),
-                                                    (300, 4096, 520, 16, True)])
+                                                    (300, 4096, 520, 16, True),
+                                                    # 150 pair tiles over 74 pairs: the last round in pieces
+                                                    (2560, 512, 3840, 0, True)])
 def test_w8a8_products_are_the_recipe(ctx, m, k, n, group, per_column):
     rng, a = recipe_inputs(m, k, m + k + n)
     q = np.rint((rng.random((k, n), dtype=np.float32) - 0.5) * 254).astype(np.int8)
