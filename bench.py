@@ -396,16 +396,21 @@ def run_colpar(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    fused = None
+    fused = fused_mc = None
     if world > 1:
+        bias_dev = torch.from_numpy(case.bias.view(np.int16)).cuda().view(torch.bfloat16)
         fused = parallel.FusedColumnParallelLinear(ctx, case.codes_nk, case.kind, case.scales, case.n, case.m,
-                                                   published_nk=True,
-                                                   bias=torch.from_numpy(case.bias.view(np.int16)).cuda()
-                                                   .view(torch.bfloat16))
+                                                   published_nk=True, bias=bias_dev, multicast=False)
+        fused_mc = parallel.FusedColumnParallelLinear(ctx, case.codes_nk, case.kind, case.scales, case.n, case.m,
+                                                      published_nk=True, bias=bias_dev, multicast=True)
+        if not fused_mc.uses_multicast:
+            fused_mc.close()
+            fused_mc = None
     with ClockSampler(local) as clocks:
         ms_gather = timed([product, gather])
         ms_local = timed([product])
         ms_fused = timed([lambda: fused(x)]) if fused is not None else None
+        ms_fused_mc = timed([lambda: fused_mc(x)]) if fused_mc is not None else None
     ctx.poll_errors()
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -422,14 +427,23 @@ def run_colpar(args):
                                  {"value": case.flops / (ms_fused / 1e3) / 1e12, "ms_per_step": ms_fused,
                                   "path": "sc_linear_allgather (product epilogue stores every tile to every rank "
                                           "over NVLink) + sc_allgather_wait"}),
+                "fused_gather_multicast": (None if ms_fused_mc is None else
+                                           {"value": case.flops / (ms_fused_mc / 1e3) / 1e12, "ms_per_step": ms_fused_mc,
+                                            "path": "sc_linear_allgather_mc (one multimem store per piece to the outputs' "
+                                                    "NVLink multicast address) + sc_allgather_wait"}),
                 "gather_bytes_per_rank": int(case.m * width * 2 * (world - 1)),
                 "roofline": {"bound": "tensor", "achieved": value / world, "peak": peaks["bf16_tflops"],
                              "unit": "TFLOP/s", "frac": value / world / peaks["bf16_tflops"], "traffic": None,
                              "peak_source": peak_src},
                 "clocks": clocks.summary(), "gpu_launches": args.steps * (2 if case.m >= 1536 else 1)}
         print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
     if fused is not None:
         fused.close()
+    if fused_mc is not None:
+        fused_mc.close()
     w.close()
     ctx.close()
     if world > 1:

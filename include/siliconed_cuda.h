@@ -282,6 +282,17 @@ SC_API sc_status sc_linear_allgather(sc_ctx* ctx, const sc_weight* w, const sc_b
                                      size_t workspace_bytes, void* stream);
 SC_API sc_status sc_allgather_wait(sc_ctx* ctx, const uint32_t* flags, int world, uint32_t epoch, void* stream);
 
+/* sc_linear_allgather with the outputs bound to an NVLink multicast object: y_multicast is the multicast
+ * address of this call's output buffer (the same offsets as every rank's y_peers[r]), and each 16-byte
+ * piece leaves the GPU once (multimem.st; NVSwitch delivers it to every rank) instead of once per rank.
+ * y_peers is still given (checked) and the flags are raised as in sc_linear_allgather.  NULL y_multicast:
+ * sc_linear_allgather.  No counterpart in the reference. */
+SC_API sc_status sc_linear_allgather_mc(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m,
+                                        const sc_bf16* bias, void* y_multicast, void* const* y_peers,
+                                        uint32_t* const* flag_peers, int world, int rank, int64_t col0,
+                                        int64_t n_total, uint32_t epoch, void* workspace, size_t workspace_bytes,
+                                        void* stream);
+
 /* CUDA IPC plumbing for the peer pointers (no counterpart in the reference): the 64-byte handle of the
  * device allocation holding device_ptr in this process and device_ptr's offset in it; the same address
  * mapped in another process (peer access enabled); the unmap (the pointer and offset sc_ipc_open took). */

@@ -56,6 +56,8 @@ SIGNATURES = {
     "sc_rotate_activation": (_I, [_P, _P, _I64, _I64, _I, _P, _P]),
     "sc_linear_ex_noalloc": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P]),
     "sc_linear_allgather": (_I, [_P, _P, _P, _I64, _P, _P, _P, _I, _I, _I64, _I64, ctypes.c_uint32, _P, _SZ, _P]),
+    "sc_linear_allgather_mc": (_I, [_P, _P, _P, _I64, _P, _P, _P, _P, _I, _I, _I64, _I64, ctypes.c_uint32, _P, _SZ,
+                                    _P]),
     "sc_allgather_wait": (_I, [_P, _P, _I, ctypes.c_uint32, _P]),
     "sc_ipc_handle": (_I, [_P, _P, _P, ctypes.POINTER(_SZ)]),
     "sc_ipc_open": (_I, [_P, _P, _SZ, ctypes.POINTER(ctypes.c_void_p)]),

@@ -737,6 +737,14 @@ sc_status sc_gemv_w8(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
 sc_status sc_linear_allgather(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
                               void* const* y_peers, uint32_t* const* flag_peers, int world, int rank, int64_t col0,
                               int64_t n_total, uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream) {
+  return sc_linear_allgather_mc(ctx, w, x, m, bias, nullptr, y_peers, flag_peers, world, rank, col0, n_total, epoch,
+                                workspace, workspace_bytes, stream);
+}
+
+sc_status sc_linear_allgather_mc(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
+                                 void* y_multicast, void* const* y_peers, uint32_t* const* flag_peers, int world,
+                                 int rank, int64_t col0, int64_t n_total, uint32_t epoch, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
   if (ctx == nullptr) return SC_INVALID_ARG;
   if (w == nullptr || x == nullptr || y_peers == nullptr || flag_peers == nullptr || m < 1)
     return fail(ctx, SC_INVALID_ARG, "null argument or m < 1");
@@ -761,6 +769,8 @@ sc_status sc_linear_allgather(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x,
   if (workspace == nullptr || workspace_bytes < rx + widened_bytes(w) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return fail(ctx, SC_WORKSPACE_TOO_SMALL,
                 "the fused gather needs a 256-byte aligned workspace of n_pad * k_pad * 2 bytes (+ the rotated x)");
+  if (reinterpret_cast<uintptr_t>(y_multicast) & 15u) return fail(ctx, SC_UNALIGNED, "the multicast output must be 16-byte aligned");
+  peers.y_mc = y_multicast;
   peers.world = world;
   peers.rank = rank;
   peers.col0 = col0;

@@ -355,10 +355,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (grow >= M || col >= N) continue;
                 const uint4 v = st[rr * 8 + (cu ^ (rr & 7))];
                 if (kPeers) {
-                  if (col + 8 <= N)
-                    for (int r = 0; r < peers.world; ++r)
-                      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(peers.y[r]) +
-                                                static_cast<int64_t>(grow) * peers.ld + peers.col0 + col) = v;
+                  const int64_t off = static_cast<int64_t>(grow) * peers.ld + peers.col0 + col;
+                  if (col + 8 <= N) {
+                    if (peers.y_mc != nullptr)
+                      multimem_st_v4(static_cast<uint16_t*>(peers.y_mc) + off, v);
+                    else
+                      for (int r = 0; r < peers.world; ++r) *reinterpret_cast<uint4*>(static_cast<uint16_t*>(peers.y[r]) + off) = v;
+                  }
                 } else {
                   uint16_t* dst = static_cast<uint16_t*>(y_out) + static_cast<int64_t>(grow) * N + col;
                   if (col + 8 <= N) {

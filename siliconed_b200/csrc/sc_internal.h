@@ -98,6 +98,7 @@ cudaError_t launch_gemm_bf16(const CUtensorMap& tmap_x, const CUtensorMap& tmap_
 constexpr int kMaxPeers = 8;
 struct PeerOut {
   void* y[kMaxPeers];
+  void* y_mc;  // the outputs' NVLink multicast address (NVSwitch copies one store to every rank), or null
   uint32_t* flags[kMaxPeers];
   int world, rank;
   int64_t col0, ld;

@@ -123,6 +123,14 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
   nt = t / rows;
 }
 
+// One 16-byte store to a multicast address: NVSwitch delivers it to the same offset of every GPU bound
+// to the multicast object (the bits are moved, not converted).
+__device__ __forceinline__ void multimem_st_v4(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(__uint_as_float(v.x)),
+               "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)), "f"(__uint_as_float(v.w))
+               : "memory");
+}
+
 // 16-byte global load cached in L2 only (data this kernel also writes: not the read-only path).
 __device__ __forceinline__ float4 ld_cg_f4(const float* p) {
   float4 v;

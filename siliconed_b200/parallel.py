@@ -115,7 +115,7 @@ class FusedColumnParallelLinear:
     """
 
     def __init__(self, ctx, codes, kind: int, scales, n: int, m_max: int, *, published_nk: bool = False,
-                 bias=None, group=None, stream=None):
+                 bias=None, group=None, stream=None, multicast: bool = True):
         import ctypes
         from . import abi
         from .products import QuantizedWeight
@@ -134,12 +134,23 @@ class FusedColumnParallelLinear:
         self.bias = None if bias is None else bias[self.n0:self.n1].contiguous()
         dev = torch.device("cuda", ctx.device)
         self.m_max = m_max
-        self.y = [torch.empty((m_max, n), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        # The outputs in symmetric memory bound to an NVLink multicast object when the system has one
+        # (torch's symmetric memory; one multimem store reaches every rank), else in ordinary device memory
+        # whose peers open it through CUDA IPC.
+        self.mc = [0, 0]
+        self._symm = None
+        if multicast:
+            self._try_multicast(dev, m_max, n)
+        if self._symm is None:
+            self.y = [torch.empty((m_max, n), dtype=torch.bfloat16, device=dev) for _ in range(2)]
         self.flags = torch.zeros(self.world, dtype=torch.int32, device=dev)
         self.ws = torch.empty(max(self.w.workspace_bytes(max(m_max, 1536)), 256), dtype=torch.uint8, device=dev)
         lib = ctx.lib
         mine = []
-        for t in (self.y[0], self.y[1], self.flags):
+        for i, t in enumerate((self.y[0], self.y[1], self.flags)):
+            if i < 2 and self._symm is not None:     # symmetric memory: no IPC handle needed (nor possible)
+                mine.append((b"", 0))
+                continue
             h = (ctypes.c_uint8 * 64)()
             off = ctypes.c_size_t()
             ctx.check(lib.sc_ipc_handle(ctx.ptr, ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off)))
@@ -151,9 +162,12 @@ class FusedColumnParallelLinear:
         self.peer_flags = [0] * self.world
         for r, handles in enumerate(everyone):
             ptrs = []
-            for (h, off), t in zip(handles, (self.y[0], self.y[1], self.flags)):
+            for i, ((h, off), t) in enumerate(zip(handles, (self.y[0], self.y[1], self.flags))):
                 if r == self.rank:
                     ptrs.append(t.data_ptr())
+                    continue
+                if i < 2 and self._symm is not None:   # symmetric memory: the peers' addresses are known
+                    ptrs.append(int(self._symm[1].buffer_ptrs[r]) + i * self.y[0].numel() * 2)
                     continue
                 p = ctypes.c_void_p()
                 buf = (ctypes.c_uint8 * 64).from_buffer_copy(h)
@@ -166,6 +180,25 @@ class FusedColumnParallelLinear:
         self.epoch = 0
         dist.barrier(group=group)
 
+    def _try_multicast(self, dev, m_max: int, n: int) -> None:
+        try:
+            import torch.distributed._symmetric_memory as symm
+            t = symm.empty((2, m_max, n), dtype=torch.bfloat16, device=dev)
+            h = symm.rendezvous(t, self.group if self.group is not None else dist.group.WORLD)
+            ok = bool(h.has_multicast_support(symm.DeviceType.CUDA, dev.index)) and int(h.multicast_ptr) != 0
+        except Exception:  # no symmetric memory or no multicast here: the IPC path
+            ok, t, h = False, None, None
+        flags = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN, group=self.group)   # every rank takes the same path
+        if int(flags.item()) == 1:
+            self._symm = (t, h)
+            self.y = [t[0], t[1]]
+            self.mc = [int(h.multicast_ptr), int(h.multicast_ptr) + m_max * n * 2]
+
+    @property
+    def uses_multicast(self) -> bool:
+        return self._symm is not None
+
     def __call__(self, x: torch.Tensor, stream=None) -> torch.Tensor:
         import ctypes
         m = x.shape[0]
@@ -176,9 +209,10 @@ class FusedColumnParallelLinear:
         lib, ctx = self.ctx.lib, self.ctx
         st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream if stream is None else stream.cuda_stream)
         b = None if self.bias is None else ctypes.c_void_p(self.bias.data_ptr())
-        ctx.check(lib.sc_linear_allgather(ctx.ptr, self.w.ptr, ctypes.c_void_p(x.data_ptr()), m, b, self._y_arr[buf],
-                                          self._f_arr, self.world, self.rank, self.n0, self.n, self.epoch,
-                                          ctypes.c_void_p(self.ws.data_ptr()), self.ws.numel(), st))
+        ctx.check(lib.sc_linear_allgather_mc(ctx.ptr, self.w.ptr, ctypes.c_void_p(x.data_ptr()), m, b,
+                                             ctypes.c_void_p(self.mc[buf]), self._y_arr[buf], self._f_arr, self.world,
+                                             self.rank, self.n0, self.n, self.epoch,
+                                             ctypes.c_void_p(self.ws.data_ptr()), self.ws.numel(), st))
         ctx.check(lib.sc_allgather_wait(ctx.ptr, ctypes.c_void_p(self.flags.data_ptr()), self.world, self.epoch, st))
         return self.y[buf][:m]
 
@@ -188,4 +222,6 @@ class FusedColumnParallelLinear:
         for p, off in self._opened:
             self.ctx.lib.sc_ipc_close(self.ctx.ptr, ctypes.c_void_p(p), off)
         self._opened = []
+        self.y = None
+        self._symm = None
         self.w.close()

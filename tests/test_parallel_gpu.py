@@ -21,7 +21,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, results):
+def _worker(rank, world, port, results, multicast=False):
     import torch.distributed as dist
     from datetime import timedelta
     from siliconed_b200 import configs, parallel
@@ -35,7 +35,8 @@ def _worker(rank, world, port, results):
         case = configs.config1(m=1600, k=512, n=1000)
         bias = torch.from_numpy(case.bias.view(np.int16)).cuda().view(torch.bfloat16)
         fused = parallel.FusedColumnParallelLinear(ctx, case.codes_nk, case.kind, case.scales, case.n, 2048,
-                                                   published_nk=True, bias=bias)
+                                                   published_nk=True, bias=bias, multicast=multicast)
+        results[f"mc{rank}"] = fused.uses_multicast
         full = QuantizedWeight(ctx, case.codes_nk, case.kind, case.scales, published_nk=True)
         ok = True
         for call in range(3):
@@ -55,14 +56,17 @@ def _worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
-def test_fused_gather_matches_single_gpu_product():
+@pytest.mark.parametrize("multicast", [False, True])
+def test_fused_gather_matches_single_gpu_product(multicast):
+    """Peer stores to every rank (multicast False), or one multimem store per piece to the outputs'
+    NVLink multicast address when the system offers one (multicast True; else it takes the peer path)."""
     import torch.multiprocessing as mp
     world = 2
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     results = manager.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, results, multicast)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -71,4 +75,7 @@ def test_fused_gather_matches_single_gpu_product():
         if p.is_alive():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    assert dict(results) == {0: True, 1: True}
+    got = dict(results)
+    assert got[0] is True and got[1] is True, got
+    assert got["mc0"] == got["mc1"] and (multicast or not got["mc0"]), got
+    print("multicast outputs:", got["mc0"])
