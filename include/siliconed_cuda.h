@@ -230,6 +230,22 @@ SC_API sc_status sc_linear_host(sc_ctx* ctx, const sc_weight* w, const sc_bf16* 
                                 void* y_host, sc_out_type y_type, sc_bf16* x_dev, void* y_dev, void* workspace,
                                 size_t workspace_bytes, int64_t chunk_rows, void* stream);
 
+/*
+ * The q / k / v product of a DiT block with QK-norm and RoPE in its epilogue (no counterpart in the
+ * reference, which runs them as a pass of their own: Block.swift, QwenImage21.swift).  W's N is
+ * 3 * heads * 128 (q, then k, then v, head after head); row r of x is token r % tokens of image
+ * r / tokens.  q and k heads: v * inv * norm[d] with inv = 1 / sqrt(sum(v^2) / 128 + eps) over the head's
+ * fp32 values, then RoPE on adjacent pairs (e0 c - e1 s, e0 s + e1 c), (c, s) = freqs[pos][d / 2][0..1],
+ * pos = offset + r % tokens; v heads as they are.  Each head is written bf16 to out[image][head][pos][0..127]
+ * of q, k or v, [images, heads, joint, 128] (the attention's layout).  norm_q / norm_k: fp32 [128]; freqs:
+ * fp32 [joint][64][2].  Takes m > 128 rows and the workspace of sc_linear_epilogue.
+ */
+SC_API sc_status sc_linear_qk_norm_rope(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m,
+                                        const sc_bf16* bias, sc_bf16* q, sc_bf16* k, sc_bf16* v, int heads,
+                                        int64_t tokens, int64_t joint, int64_t offset, const float* norm_q,
+                                        const float* norm_k, const float* freqs, float eps, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
 /* sc_linear_ex with its scratch in a 32 MiB device array of the library instead of a workspace: it
  * allocates nothing and takes no workspace argument.  No counterpart in the reference: it serves
  * callers that have no scratch buffer to pass (a binding that keeps the signature of

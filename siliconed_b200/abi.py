@@ -49,6 +49,8 @@ SIGNATURES = {
     "sc_linear_ex": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _SZ, _P]),
     "sc_linear_epilogue": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _P, _SZ, _P]),
     "sc_weight_set_rotation": (_I, [_P, _P, _I]),
+    "sc_linear_qk_norm_rope": (_I, [_P, _P, _P, _I64, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P, _P, _P,
+                                    ctypes.c_float, _P, _SZ, _P]),
     "sc_linear_host": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _P, _P, _SZ, _I64, _P]),
     "sc_w8a8_workspace_size": (_I, [_P, _P, _I64, ctypes.POINTER(_SZ)]),
     "sc_linear_w8a8": (_I, [_P, _P, _P, _I, _I64, _P, _P, _I, _P, _SZ, _P]),

@@ -685,6 +685,52 @@ sc_status sc_linear_host(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x_host,
   return check_cuda(ctx, cudaStreamWaitEvent(st, ev_end, 0), "stream wait");
 }
 
+sc_status sc_linear_qk_norm_rope(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
+                                 sc_bf16* q, sc_bf16* k, sc_bf16* v, int heads, int64_t tokens, int64_t joint,
+                                 int64_t offset, const float* norm_q, const float* norm_k, const float* freqs,
+                                 float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  sc_status s = check_product_args(ctx, w, x, m, bias, q);
+  if (s != SC_OK) return s;
+  if (m == 0) return SC_OK;
+  if (heads < 1 || w->n != 3LL * heads * 128) return fail(ctx, SC_UNSUPPORTED_SHAPE, "N must be 3 * heads * 128");
+  if (tokens < 1 || m % tokens != 0 || offset < 0 || joint < offset + tokens || joint > 0x7FFFFFFF)
+    return fail(ctx, SC_INVALID_ARG, "m must be images * tokens and offset + tokens <= joint");
+  if (k == nullptr || v == nullptr || norm_q == nullptr || norm_k == nullptr || freqs == nullptr)
+    return fail(ctx, SC_INVALID_ARG, "null output, norm weight or frequency table");
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u ||
+      (reinterpret_cast<uintptr_t>(norm_q) | reinterpret_cast<uintptr_t>(norm_k) | reinterpret_cast<uintptr_t>(freqs)) & 3u)
+    return fail(ctx, SC_UNALIGNED, "q, k, v must be 16-byte aligned, the fp32 tables 4-byte aligned");
+  if (!is_device_pointer(k) || !is_device_pointer(v) || !is_device_pointer(norm_q) || !is_device_pointer(norm_k) ||
+      !is_device_pointer(freqs))
+    return fail(ctx, SC_INVALID_ARG, "outputs and tables must be device memory");
+  if (m <= kPairMinRows) return fail(ctx, SC_UNSUPPORTED_SHAPE, "sc_linear_qk_norm_rope takes more than 128 rows");
+  const size_t rx = w->rotation != 0 ? rotated_x_bytes(m, w->k) : 0;
+  if (workspace == nullptr || workspace_bytes < rx + widened_bytes(w) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(ctx, SC_WORKSPACE_TOO_SMALL,
+                "sc_linear_qk_norm_rope needs a 256-byte aligned workspace of n_pad * k_pad * 2 bytes (+ the rotated x)");
+  if ((s = enter(ctx)) != SC_OK) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((s = rotate_operand(ctx, w, x, m, workspace, workspace_bytes, st)) != SC_OK) return s;
+  CUtensorMap tmx, tmw;
+  if ((s = make_tmap_x(ctx, x, m, w->k, &tmx)) != SC_OK) return s;
+  if ((s = make_tmap_widened(ctx, w, workspace, &tmw)) != SC_OK) return s;
+  if ((s = check_cuda(ctx, launch_widen(w, workspace, ctx->sm_count, st), "widen launch")) != SC_OK) return s;
+  HeadOut ho;
+  ho.q = q;
+  ho.k = k;
+  ho.v = v;
+  ho.norm_q = norm_q;
+  ho.norm_k = norm_k;
+  ho.freqs = freqs;
+  ho.eps = eps;
+  ho.heads = heads;
+  ho.tokens = static_cast<int>(tokens);
+  ho.joint = static_cast<int>(joint);
+  ho.offset = static_cast<int>(offset);
+  return check_cuda(ctx, launch_gemm_bf16_heads(tmx, tmw, w, bias, ho, m, ctx->d_err, ctx->sm_count, st),
+                    "qk-norm gemm launch");
+}
+
 sc_status sc_linear_epilogue(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,
                              void* y, sc_epilogue op, const float* gate, void* workspace, size_t workspace_bytes,
                              void* stream) {

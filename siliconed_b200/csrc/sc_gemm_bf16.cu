@@ -64,7 +64,12 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 // kOp: the epilogue's operation after v = acc * scale + bias (fp32).  kOpNone stores v; kOpGelu stores
 // bf16(gelu_tanh(v)) (one rounding, where a separate pass would round v first); kOpResidual adds
 // gate[n] * v to the fp32 output in place, x = fma(gate, v, x) (the gated residual stream).
-constexpr int kOpNone = 0, kOpGelu = 1, kOpResidual = 2;
+// kOpQkRope: the q / k / v product of a DiT block; each 128-column half of a tile is one head of q, k or
+// v.  For q and k the head is RMS-normalised over its 128 values (sum of squares from a first pass over
+// the accumulator, inv = 1 / sqrt(ss / 128 + eps), then * inv * norm[d]) and rotated by RoPE on adjacent
+// pairs, (e0 c - e1 s, e0 s + e1 c) with (c, s) = freqs[pos][d / 2]; v is stored as it is.  Every head
+// goes to its [batch, heads, joint, 128] row: the attention's layout, written once.
+constexpr int kOpNone = 0, kOpGelu = 1, kOpResidual = 2, kOpQkRope = 3;
 
 // gelu_tanh(v) = 0.5 v (1 + tanh(u)), u = sqrt(2 / pi) (v + 0.044715 v^3), through the identity
 // 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)): one exponential and one approximate division, about 2e-6
@@ -95,7 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const float* __restrict__ scales, const uint16_t* __restrict__ bias, void* __restrict__ y_out,
                    int M, int N, int k_tiles, int m_tiles, int n_tiles, int* err,
                    const __grid_constant__ PeerOut peers, const float* __restrict__ gate,
-                   const float* __restrict__ row_scales) {
+                   const float* __restrict__ row_scales, const __grid_constant__ HeadOut ho) {
   static_assert(kOp != kOpResidual || kF32Out, "the residual is fp32");
   static_assert(kOp != kOpGelu || !kF32Out, "the GELU output is bf16");
   static_assert(!kI8 || (kOp == kOpNone && !kPeers), "W8A8 stores plain outputs");
@@ -256,8 +261,90 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__shfl_sync(0xFFFFFFFFu, ready, 0)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if (kOp == kOpQkRope) {
+        const int hd = ho.heads * 128;
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
+        for (int hh = 0; hh < BN / 128; ++hh) {
+          const int cb = n0 + hh * 128;
+          if (cb >= N) break;
+          const int which = cb / hd, head = (cb % hd) / 128;
+          const uint32_t tb = tbase + hh * 128;
+          float inv = 1.0f;
+          if (which < 2) {
+            float ss = 0.0f;
+#pragma unroll 1
+            for (int ch = 0; ch < 4; ++ch) {
+              uint32_t r[32];
+              tmem_ld_32(tb + ch * 32, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float v = epi_value<false>(r[j], s_scale[hh * 128 + ch * 32 + j], s_bias[hh * 128 + ch * 32 + j],
+                                                 0.0f, true);
+                ss = __fmaf_rn(v, v, ss);
+              }
+            }
+            inv = 1.0f / sqrtf(ss / 128.0f + ho.eps);
+          }
+          const float* wn = which == 0 ? ho.norm_q : ho.norm_k;
+          const int tok = row % ho.tokens;
+          const float* fr = ho.freqs + static_cast<int64_t>(ho.offset + tok) * 128;
+          uint16_t* out = which == 0 ? ho.q : (which == 1 ? ho.k : ho.v);
+#pragma unroll 1
+          for (int ch = 0; ch < 4; ++ch) {
+            uint32_t r[32];
+            tmem_ld_32(tb + ch * 32, r);
+            tmem_wait_ld();
+            uint32_t packed[16];
+            const bool rope = which < 2 && row < M;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const int d = ch * 32 + j;
+              // two pairs per step: 16-byte loads of the norm weights (the same for the warp) and of the
+              // row's (cos, sin) pairs
+              const float4 wv = rope ? *reinterpret_cast<const float4*>(wn + d) : make_float4(1.f, 1.f, 1.f, 1.f);
+              const float4 fv = rope ? *reinterpret_cast<const float4*>(fr + d) : make_float4(1.f, 0.f, 1.f, 0.f);
+              float e[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                e[i] = epi_value<false>(r[j + i], s_scale[hh * 128 + d + i], s_bias[hh * 128 + d + i], 0.0f, true);
+              if (rope) {
+                const float a0 = e[0] * inv * wv.x, a1 = e[1] * inv * wv.y;
+                const float a2 = e[2] * inv * wv.z, a3 = e[3] * inv * wv.w;
+                e[0] = a0 * fv.x - a1 * fv.y;
+                e[1] = a0 * fv.y + a1 * fv.x;
+                e[2] = a2 * fv.z - a3 * fv.w;
+                e[3] = a2 * fv.w + a3 * fv.z;
+              }
+              const __nv_bfloat162 h0 = __floats2bfloat162_rn(e[0], e[1]), h1 = __floats2bfloat162_rn(e[2], e[3]);
+              packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h0);
+              packed[j / 2 + 1] = *reinterpret_cast<const uint32_t*>(&h1);
+            }
+            // two chunks (64 values of the head) per flush: 8 lanes write 128 contiguous bytes of a row
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              st[lane * 8 + (((ch & 1) * 4 + q) ^ (lane & 7))] =
+                  make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+            if (ch & 1) {
+              __syncwarp();
+#pragma unroll
+              for (int it = 0; it < 8; ++it) {
+                const int u = it * 32 + lane, rr = u >> 3, cu = u & 7;
+                const int grow = row0 + rr;
+                if (grow < M) {
+                  const int b = grow / ho.tokens, t = grow % ho.tokens;
+                  uint16_t* dst = out + ((static_cast<int64_t>(b) * ho.heads + head) * ho.joint + ho.offset + t) * 128 +
+                                  (ch - 1) * 32 + cu * 8;
+                  *reinterpret_cast<uint4*>(dst) = st[rr * 8 + (cu ^ (rr & 7))];
+                }
+              }
+              __syncwarp();
+            }
+          }
+        }
+      }
+#pragma unroll 1
+      for (int ch = 0; ch < (kOp == kOpQkRope ? 0 : BN / 32); ++ch) {
         float4 xnext[8];
         if (kOp == kOpResidual && res_fast && ch + 1 < BN / 32) {
 #pragma unroll
@@ -446,7 +533,8 @@ __global__ void __launch_bounds__(256) widen_codes(const uint4* __restrict__ cod
 template <bool kF32Out, bool kPeers, int kOp = kOpNone, bool kI8 = false>
 cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const sc_weight* w, const uint16_t* bias,
                         void* y, int64_t m, int* err, int sm_count, cudaStream_t stream, const PeerOut& peers,
-                        const float* gate = nullptr, const float* row_scales = nullptr) {
+                        const float* gate = nullptr, const float* row_scales = nullptr, const HeadOut* heads = nullptr) {
+  const HeadOut ho = heads != nullptr ? *heads : HeadOut{};
   auto kernel = gemm_bf16_pair<kF32Out, kPeers, kOp, kI8>;
   static bool configured = false;
   if (!configured) {
@@ -477,7 +565,7 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias, y,
                             static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers, gate,
-                            row_scales);
+                            row_scales, ho);
 }
 
 // The weight's arena codes (int8 stored biased by 128) made signed again for the int8 MMA: code ^ 0x80.
@@ -540,6 +628,14 @@ cudaError_t launch_gemm_bf16(const CUtensorMap& tmap_x, const CUtensorMap& tmap_
   const PeerOut none = {};
   return f32_out ? gemm_bf16::launch_gemm<true, false>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream, none)
                  : gemm_bf16::launch_gemm<false, false>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream, none);
+}
+
+cudaError_t launch_gemm_bf16_heads(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
+                                   const uint16_t* bias, const HeadOut& heads, int64_t m, int* err, int sm_count,
+                                   cudaStream_t stream) {
+  const PeerOut none = {};
+  return gemm_bf16::launch_gemm<false, false, gemm_bf16::kOpQkRope>(tmap_x, tmap_w, w, bias, nullptr, m, err, sm_count,
+                                                                    stream, none, nullptr, nullptr, &heads);
 }
 
 cudaError_t launch_gemm_bf16_peers(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,

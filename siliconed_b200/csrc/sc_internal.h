@@ -105,6 +105,18 @@ struct PeerOut {
   uint32_t epoch;
   int* counter;
 };
+// The q / k / v product's outputs when QK-norm and RoPE run in its epilogue (sc_linear_qk_norm_rope):
+// q, k, v [batch, heads, joint, 128] bf16; the product's row r is token r % tokens of image r / tokens,
+// at position offset + r % tokens of the joint sequence; freqs [joint][64][2] (cos, sin) per position.
+struct HeadOut {
+  uint16_t *q, *k, *v;
+  const float *norm_q, *norm_k, *freqs;
+  float eps;
+  int heads, tokens, joint, offset;
+};
+cudaError_t launch_gemm_bf16_heads(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
+                                   const uint16_t* bias, const HeadOut& heads, int64_t m, int* err, int sm_count,
+                                   cudaStream_t stream);
 cudaError_t launch_gemm_bf16_peers(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
                                    const uint16_t* bias, const PeerOut& peers, int64_t m, int* err, int sm_count,
                                    cudaStream_t stream);

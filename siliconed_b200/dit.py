@@ -29,8 +29,9 @@ from . import abi
 from . import dit_abi as dk
 from .products import Context, QuantizedWeight
 
-# The MMDiT block's GELU and gated residuals run inside the epilogue of the product before them
-# (sc_linear_epilogue) for products of at least FUSE_MIN_ROWS rows.
+# From FUSE_MIN_ROWS rows the blocks run QK-norm + RoPE in the q / k / v product's epilogue
+# (sc_linear_qk_norm_rope), and the MMDiT block its GELU and gated residuals in the epilogues of the
+# products before them (sc_linear_epilogue).
 FUSED_EPILOGUES = True
 FUSE_MIN_ROWS = 1536
 
@@ -70,6 +71,18 @@ class Linear:
             return self.weight.linear_epilogue(x, out, abi.EPI_GELU_TANH, bias=self.bias, workspace=workspace)
         self(x, out, workspace)
         return dk.gelu_tanh(out)
+
+    def qkv_heads(self, x: torch.Tensor, q, k, v, norm_q, norm_k, freqs, eps: float, batch: int, tokens: int,
+                  offset: int, scratch: torch.Tensor, workspace=None) -> None:
+        """q / k / v [batch, heads, joint, 128] of the q / k / v product, QK-norm and RoPE applied: in the
+        product's epilogue from FUSE_MIN_ROWS rows (sc_linear_qk_norm_rope), else the product into `scratch`
+        (bf16 [rows, 3 d]) and sd_qk_norm_rope."""
+        if self._fuse(x.shape[0]):
+            self.weight.linear_qk_norm_rope(x, q, k, v, norm_q, norm_k, freqs, eps, tokens, offset, bias=self.bias,
+                                            workspace=workspace)
+            return
+        self(x, scratch, workspace)
+        dk.qk_norm_rope(scratch, batch, tokens, q.shape[1], norm_q, norm_k, freqs, eps, q, k, v, q.shape[2], offset)
 
     def gated_residual(self, x: torch.Tensor, resid: torch.Tensor, gate: torch.Tensor, scratch: torch.Tensor,
                        workspace=None) -> torch.Tensor:
@@ -192,9 +205,8 @@ class ZImageBlock:
         scale_msa, gate_msa, scale_mlp, gate_mlp = mod[0], mod[1], mod[2], mod[3]
         # attention
         dk.rms_norm_modulate(x, self.norm1, scale_msa, self.eps, b["a"])
-        self.qkv(b["a"], b["qkv"], ws)
-        dk.qk_norm_rope(b["qkv"], 1, s, self.heads, self.norm_q, self.norm_k, freqs, self.eps, b["q"], b["k"], b["v"],
-                        s, 0)
+        self.qkv.qkv_heads(b["a"], b["q"], b["k"], b["v"], self.norm_q, self.norm_k, freqs, self.eps, 1, s, 0, b["qkv"],
+                           ws)
         o = attention(b["q"], b["k"], b["v"])
         merged = merged_rows(o, 1, self.heads, s, 0, s, b["merged"])
         self.out(merged, b["y"], ws)
@@ -257,8 +269,7 @@ class MMDiTBlock:
             rows = x.shape[0]
             a, qkv = b["a"][:rows], b["qkv"][:rows]
             dk.layer_norm_modulate(x, m[1], m[0], self.eps, a)
-            sw.qkv(a, qkv, ws)
-            dk.qk_norm_rope(qkv, batch, n, H, sw.norm_q, sw.norm_k, freqs, self.eps, b["q"], b["k"], b["v"], joint, off)
+            sw.qkv.qkv_heads(a, b["q"], b["k"], b["v"], sw.norm_q, sw.norm_k, freqs, self.eps, batch, n, off, qkv, ws)
         o = attention(b["q"], b["k"], b["v"])
         for (sw, x, n, off), m in zip(streams, mods):
             rows = x.shape[0]

@@ -217,6 +217,24 @@ class QuantizedWeight:
         after the rotated x of a convrot weight."""
         return self.workspace_bytes(max(int(m), 1536))
 
+    def linear_qk_norm_rope(self, x, q, k, v, norm_q, norm_k, freqs, eps: float, tokens: int, offset: int = 0,
+                            bias=None, workspace=None, stream=None):
+        """sc_linear_qk_norm_rope: the q / k / v product with QK-norm and RoPE in its epilogue, written to
+        q, k, v (bf16 [images, heads, joint, 128]); x's rows are images x tokens, at joint positions
+        offset + token."""
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.shape[1] != self.k:
+            raise SiliconedError(abi.INVALID_ARG, f"x must be a CUDA bf16 [M, {self.k}] tensor")
+        m = x.shape[0]
+        heads, joint = q.shape[1], q.shape[2]
+        if workspace is None:
+            workspace = self.ctx.workspace(self.epilogue_workspace_bytes(m), x.device)
+        ws_bytes = workspace.numel() * workspace.element_size()
+        self.ctx.check(self.ctx.lib.sc_linear_qk_norm_rope(
+            self.ctx.ptr, self.ptr, _ptr(x), m, _ptr(bias), _ptr(q), _ptr(k), _ptr(v), heads, int(tokens), joint,
+            int(offset), _ptr(norm_q), _ptr(norm_k), _ptr(freqs), float(eps), _ptr(workspace), ws_bytes,
+            _stream_ptr(stream)))
+        return q, k, v
+
     def linear_epilogue(self, x, out, op: int, bias=None, gate=None, workspace=None, stream=None):
         """sc_linear_epilogue: v = (x . q) * s + bias with the DiT stage `op` fused into the product's
         epilogue.  EPI_GELU_TANH: out bf16 [M, N] = gelu_tanh(v); EPI_GATED_RESIDUAL: out fp32 [M, N]

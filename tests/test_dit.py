@@ -326,3 +326,43 @@ def test_mmdit_block_with_fused_epilogues_matches_fp32_reference():
     assert rel(x_img, refs[1]) <= 1e-2, rel(x_img, refs[1])
     model.close()
     ctx.close()
+
+
+@gpu
+@needs_cuda
+def test_qk_norm_rope_in_the_product_epilogue():
+    """From 1536 rows the q / k / v product writes the attention's q, k, v itself (sc_linear_qk_norm_rope):
+    v bit for bit as the product plus sd_qk_norm_rope, q and k within the bf16 rounding that the separate
+    pass applies to its input first (relative L2 <= 5e-3, worst element <= 2 % of the largest)."""
+    import siliconed_b200.dit as dit
+    from siliconed_b200.products import Context
+    ctx = Context(0)
+    g = torch.Generator(device="cuda").manual_seed(13)
+    heads, batch, tokens, joint, off = 2, 2, 1600, 1800, 200
+    lin = dit.Linear(ctx, 3 * heads * 128, 256, g)
+    x = torch.randn(batch * tokens, 256, generator=g, device="cuda").to(torch.bfloat16)
+    norm_q = (1 + 0.1 * torch.randn(128, generator=g, device="cuda")).float()
+    norm_k = (1 + 0.1 * torch.randn(128, generator=g, device="cuda")).float()
+    freqs = dit.rope_table(torch.stack([torch.arange(joint), torch.arange(joint)], dim=1)).cuda()
+    ws = torch.empty(lin.workspace_bytes(batch * tokens), dtype=torch.uint8, device="cuda")
+    scratch = torch.empty(batch * tokens, 3 * heads * 128, dtype=torch.bfloat16, device="cuda")
+    outs = {}
+    try:
+        for fused in (True, False):
+            dit.FUSED_EPILOGUES = fused
+            q, k, v = (torch.zeros(batch, heads, joint, 128, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+            lin.qkv_heads(x, q, k, v, norm_q, norm_k, freqs, 1e-6, batch, tokens, off, scratch, ws)
+            outs[fused] = (q, k, v)
+    finally:
+        dit.FUSED_EPILOGUES = True
+    torch.cuda.synchronize()
+    ctx.poll_errors()
+    (qf, kf, vf), (qu, ku, vu) = outs[True], outs[False]
+    assert torch.equal(vf, vu)
+    assert not vf[:, :, :off].any() and vf[:, :, off:].any()
+    for a, b in ((qf, qu), (kf, ku)):
+        a, b = a.float(), b.float()
+        assert rel(a, b) <= 5e-3, rel(a, b)
+        assert float((a - b).abs().max()) <= 0.02 * float(b.abs().max())
+    lin.close()
+    ctx.close()
