@@ -46,7 +46,7 @@ def load_peaks():
 
 def make_case(workload: str):
     from siliconed_b200 import configs
-    if workload == "cfg1":
+    if workload in ("cfg1", "cfg1-w8a8"):
         return configs.config1()
     if workload == "cfg2":
         return configs.config2()
@@ -212,12 +212,17 @@ def run_ours(args):
 
     case = make_case(args.workload)
     metric, unit = metric_of(case)
+    # cfg1-w8a8: config 1's data through the W8A8 route (x quantized to int8 per row, int8 x int8 on the
+    # tensor cores): another arithmetic than config 1's weight-only product, reported beside it.
+    w8a8 = args.workload.endswith("-w8a8")
+    if w8a8:
+        metric, unit = "W8A8 (int8 activation x int8 weight) GEMM TOP/s at M=4096", "TOP/s"
     ctx = Context(local)
     w = QuantizedWeight(ctx, case.codes_nk, case.kind, case.scales, published_nk=True)
     x = torch.from_numpy(case.x.view(np.int16)).cuda().view(torch.bfloat16)
     bias = None if case.bias is None else torch.from_numpy(case.bias.view(np.int16)).cuda().view(torch.bfloat16)
     y = torch.empty((case.m, case.n), dtype=torch.bfloat16, device="cuda")
-    ws_bytes = w.workspace_bytes(case.m)
+    ws_bytes = w.w8a8_workspace_bytes(case.m) if w8a8 else w.workspace_bytes(case.m)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     clean = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
@@ -232,7 +237,10 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
 
     def step():
-        w.linear(x, bias=bias, out=y, workspace=ws, stream=stream)
+        if w8a8:
+            w.linear_w8a8(x, y, bias=bias, workspace=ws, stream=stream)
+        else:
+            w.linear(x, bias=bias, out=y, workspace=ws, stream=stream)
 
     for _ in range(args.warmup):
         flush_l2(1)
@@ -273,15 +281,22 @@ def run_ours(args):
     y_host = torch.empty((case.m, case.n), dtype=torch.bfloat16).pin_memory()
     x_dev = torch.empty_like(x)
     e2e_steps = max(3, min(args.steps, 20))
+    def e2e_step():
+        if w8a8:   # copy in, product, copy out on one stream
+            x_dev.copy_(x_host, non_blocking=True)
+            w.linear_w8a8(x_dev, y, bias=bias, workspace=ws, stream=stream)
+            y_host.copy_(y, non_blocking=True)
+        else:
+            w.linear_host(x_host, y_host, bias=bias, x_dev=x_dev, y_dev=y, workspace=ws, stream=stream)
     for _ in range(2):
-        w.linear_host(x_host, y_host, bias=bias, x_dev=x_dev, y_dev=y, workspace=ws, stream=stream)
+        e2e_step()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(e2e_steps):
-        w.linear_host(x_host, y_host, bias=bias, x_dev=x_dev, y_dev=y, workspace=ws, stream=stream)
+        e2e_step()
     e1.record(stream)
     torch.cuda.synchronize()
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
@@ -295,6 +310,9 @@ def run_ours(args):
         if unit == "GB/s":
             achieved = case.bytes_moved() / sec_per_step / 1e9
             peak, runit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
+        elif w8a8:
+            achieved = case.flops / sec_per_step / 1e12
+            peak, runit, bound = 2.0 * peaks["bf16_tflops"], "TOP/s", "tensor"
         else:
             achieved = case.flops / sec_per_step / 1e12
             peak, runit, bound = peaks["bf16_tflops"], "TFLOP/s", "tensor"
@@ -307,21 +325,25 @@ def run_ours(args):
                     traffic = int(parts[1])
         line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8" if w8a8 else "bf16", "data": "synthetic",
                 "config": dict(describe(case, args.workload), parallelism=f"replicas x{world} (batch-sharded)"),
                 "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": runit,
                              "frac": achieved / peak, "traffic": traffic,
                              "peak_source": f"{peak_src} (burst figure: the kernel is timed alone)",
-                             "kernels": route_kernels(case, ws_bytes)},
+                             "kernels": (["sign_codes", "quantize_rows", "gemm_bf16_pair (kind::i8)"] if w8a8
+                                         else route_kernels(case, ws_bytes))},
                 "clocks": clocks.summary(),
                 "e2e": {"value": e2e_value, "unit": unit,
                         "h2d_bytes_per_step": int(case.x.nbytes),
                         "d2h_bytes_per_step": int(case.m * case.n * 2),
                         "path": "QuantizedWeight.linear_host (sc_linear_host): pinned host x in, y out, every step; "
                                 "copies overlapped with the products in chunks of rows"},
-                "gpu_launches": args.steps * len(route_kernels(case, ws_bytes)),
+                "gpu_launches": args.steps * (3 if w8a8 else len(route_kernels(case, ws_bytes))),
                 "step_ms_min": min(per_step), "step_ms_median": statistics.median(per_step)}
-        if not args.no_cpu_baseline and world == 1:
+        if w8a8:
+            line["roofline"]["peak_source"] += "; int8 dense peak taken as 2 x the measured bf16 figure (the nominal ratio)"
+            line["e2e"]["path"] = "QuantizedWeight.linear_w8a8 with pinned host x in and y out on one stream, every step"
+        if not args.no_cpu_baseline and world == 1 and not w8a8:
             per, flops, byts, threads, rows, reps = cpu_baseline(case)
             cv = (byts / per / 1e9) if unit == "GB/s" else (flops / per / 1e12)
             line["cpu_baseline"] = {"value": cv, "unit": unit, "cores": threads, "kind": "port",
