@@ -138,6 +138,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_barrier();  // barriers of both CTAs initialised, TMEM allocated in both
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  // Launched early behind the widening (or the int8 passes) of the same product, the set-up above
+  // overlapped their end; nothing reads or writes global memory before this point.
+  pdl_wait();
 
   if (warp == 0) {
     // ---------------- TMA producer (each CTA loads its own halves) ----------------
@@ -511,6 +514,7 @@ constexpr int kWidenPer = 4;
 template <int kKind, bool kNaN>
 __global__ void __launch_bounds__(256) widen_codes(const uint4* __restrict__ codes, uint4* __restrict__ out,
                                                     int64_t chunks) {
+  pdl_launch_dependents();  // the GEMM that reads the widened copy may set up meanwhile
   const int64_t base = static_cast<int64_t>(blockIdx.x) * (256 * kWidenPer) + threadIdx.x;
   uint4 in[kWidenPer];
 #pragma unroll
@@ -556,13 +560,17 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // The GEMM may be launched while the kernel before it (the widening) finishes: it sets up its
+  // barriers and TMEM, then waits for that kernel's writes (pdl_wait) before its first access.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias, y,
                             static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers, gate,
                             row_scales, ho);
@@ -571,6 +579,7 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
 // The weight's arena codes (int8 stored biased by 128) made signed again for the int8 MMA: code ^ 0x80.
 __global__ void __launch_bounds__(256) sign_codes(const uint4* __restrict__ codes, uint4* __restrict__ out,
                                                   int64_t chunks) {
+  pdl_launch_dependents();
   const int64_t base = static_cast<int64_t>(blockIdx.x) * (256 * kWidenPer) + threadIdx.x;
   uint4 in[kWidenPer];
 #pragma unroll

@@ -123,6 +123,13 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
   nt = t / rows;
 }
 
+// Programmatic dependent launch.  The kernel launched after this one on the stream (with the
+// programmatic-serialization attribute) may start once every CTA of this grid has issued this, or exited.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Waits until the grid this one depends on has completed and its writes are visible; returns at once for a
+// kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // One 16-byte store to a multicast address: NVSwitch delivers it to the same offset of every GPU bound
 // to the multicast object (the bits are moved, not converted).
 __device__ __forceinline__ void multimem_st_v4(void* mc, uint4 v) {

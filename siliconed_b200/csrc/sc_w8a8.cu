@@ -12,6 +12,7 @@
 #include <cuda_bf16.h>
 
 #include "sc_internal.h"
+#include "sc_ptx.cuh"
 
 namespace sc {
 namespace {
@@ -24,6 +25,7 @@ __global__ void __launch_bounds__(kQThreads)
                   float* __restrict__ scales) {
   extern __shared__ float y[];  // [k rounded up to 256]
   __shared__ float part[kQThreads / 32];
+  pdl_launch_dependents();  // the int8 GEMM after it may set up meanwhile
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (kF32In) {
