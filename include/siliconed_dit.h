@@ -63,6 +63,11 @@ SD_API int sd_attention_merge(const uint16_t* o, int batch, int heads, int head_
  * (the fused gate / up product), silu(a) = a / (1 + exp(-a)) (Ops.siluGate, Ops.swift:64-90). */
 SD_API int sd_swiglu(const uint16_t* h, int64_t rows, int hidden, uint16_t* out, void* stream);
 
+/* sd_swiglu on a product whose gate and up columns are interleaved in blocks of `block` (gate block j at
+ * h[r, 2 block j ...], up block j right after it): the layout whose SwiGLU a product can apply in its
+ * epilogue (SC_EPI_SWIGLU), used below the epilogue's row count.  block a multiple of 8 dividing hidden. */
+SD_API int sd_swiglu_blocks(const uint16_t* h, int64_t rows, int hidden, int block, uint16_t* out, void* stream);
+
 /* h = bf16( 0.5 h (1 + tanh(sqrt(2 / pi) (h + 0.044715 h^3))) ) in place, bf16 [count]
  * (nn.GELU(approximate="tanh"), QwenImage21.swift:953-963). */
 SD_API int sd_gelu_tanh(uint16_t* h, int64_t count, void* stream);

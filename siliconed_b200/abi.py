@@ -26,7 +26,7 @@ SCALE_F32, SCALE_BF16, SCALE_F16 = 1, 2, 3
 SCALE_TENSOR, SCALE_COLUMNS = 0, 1
 VALUES_ON_DEVICE, PUBLISHED_NK = 0x1, 0x2
 OUT_BF16, OUT_F32 = 0, 1
-EPI_GELU_TANH, EPI_GATED_RESIDUAL = 1, 2
+EPI_GELU_TANH, EPI_GATED_RESIDUAL, EPI_SWIGLU = 1, 2, 3
 IN_BF16, IN_F32 = 0, 1
 
 _P, _I64, _I, _U32, _SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint32, ctypes.c_size_t

@@ -342,6 +342,40 @@ int sd_swiglu(const uint16_t* h, int64_t rows, int hidden, uint16_t* out, void* 
   return status_of(cudaGetLastError());
 }
 
+// The same with gate and up interleaved in blocks of `block` columns (gate block j, then up block j).
+__global__ void swiglu_blocks_k(const uint16_t* __restrict__ hbuf, int64_t rows, int hidden, int block,
+                                uint16_t* __restrict__ out) {
+  const int64_t per_row = hidden / 8;
+  const int64_t total = rows * per_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / per_row, c = (i % per_row) * 8;
+    const int64_t src = r * 2 * hidden + (c / block) * 2 * block + c % block;
+    const uint4 a = *reinterpret_cast<const uint4*>(hbuf + src);
+    const uint4 b = *reinterpret_cast<const uint4*>(hbuf + src + block);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+    uint32_t ow[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a0 = from_bf16(static_cast<uint16_t>(aw[j])), a1 = from_bf16(static_cast<uint16_t>(aw[j] >> 16));
+      const float b0 = from_bf16(static_cast<uint16_t>(bw[j])), b1 = from_bf16(static_cast<uint16_t>(bw[j] >> 16));
+      const float s0 = a0 / (1.0f + expf(-a0)), s1 = a1 / (1.0f + expf(-a1));
+      ow[j] = pack_bf16x2(s0 * b0, s1 * b1);
+    }
+    *reinterpret_cast<uint4*>(out + r * hidden + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  }
+}
+
+int sd_swiglu_blocks(const uint16_t* h, int64_t rows, int hidden, int block, uint16_t* out, void* stream) {
+  if (h == nullptr || out == nullptr || rows < 0 || hidden <= 0 || block <= 0 || block % 8 != 0 ||
+      hidden % block != 0 || !aligned(h, 16) || !aligned(out, 16))
+    return SD_INVALID_ARG;
+  if (rows == 0) return SD_OK;
+  swiglu_blocks_k<<<grid_for(rows * (hidden / 8), 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(h, rows, hidden,
+                                                                                                   block, out);
+  return status_of(cudaGetLastError());
+}
+
 int sd_gelu_tanh(uint16_t* h, int64_t count, void* stream) {
   if (h == nullptr || count < 0 || !aligned(h, 16)) return SD_INVALID_ARG;
   if (count == 0) return SD_OK;

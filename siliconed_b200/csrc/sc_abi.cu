@@ -736,7 +736,10 @@ sc_status sc_linear_epilogue(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, 
                              void* stream) {
   sc_status s = check_product_args(ctx, w, x, m, bias, y);
   if (s != SC_OK) return s;
-  if (op != SC_EPI_GELU_TANH && op != SC_EPI_GATED_RESIDUAL) return fail(ctx, SC_INVALID_ARG, "unknown epilogue");
+  if (op != SC_EPI_GELU_TANH && op != SC_EPI_GATED_RESIDUAL && op != SC_EPI_SWIGLU)
+    return fail(ctx, SC_INVALID_ARG, "unknown epilogue");
+  if (op == SC_EPI_SWIGLU && w->n % 256 != 0)
+    return fail(ctx, SC_UNSUPPORTED_SHAPE, "SwiGLU needs N a multiple of 256 (blocks of 128 gate, 128 up)");
   if (op == SC_EPI_GATED_RESIDUAL && (gate == nullptr || !is_device_pointer(gate) ||
                                       (reinterpret_cast<uintptr_t>(gate) & 3u)))
     return fail(ctx, SC_INVALID_ARG, "the gated residual needs a 4-byte aligned device gate of n floats");

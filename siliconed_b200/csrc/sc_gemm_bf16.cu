@@ -69,7 +69,10 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 // the accumulator, inv = 1 / sqrt(ss / 128 + eps), then * inv * norm[d]) and rotated by RoPE on adjacent
 // pairs, (e0 c - e1 s, e0 s + e1 c) with (c, s) = freqs[pos][d / 2]; v is stored as it is.  Every head
 // goes to its [batch, heads, joint, 128] row: the attention's layout, written once.
-constexpr int kOpNone = 0, kOpGelu = 1, kOpResidual = 2, kOpQkRope = 3;
+// kOpSwiglu: the gate / up product of a SwiGLU MLP whose weight columns come in blocks of 128, gate block j
+// then up block j (each 256-column tile holds one pair); the epilogue stores bf16(silu(a) * b) for the
+// tile's 128 outputs, silu(a) = a / (1 + exp(-a)), into y [M, N / 2] at columns n0 / 2 ...
+constexpr int kOpNone = 0, kOpGelu = 1, kOpResidual = 2, kOpQkRope = 3, kOpSwiglu = 4;
 
 // gelu_tanh(v) = 0.5 v (1 + tanh(u)), u = sqrt(2 / pi) (v + 0.044715 v^3), through the identity
 // 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)): one exponential and one approximate division, about 2e-6
@@ -346,8 +349,48 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (kOp == kOpSwiglu) {
+        const int ldy = N / 2, c0 = n0 / 2;
 #pragma unroll 1
-      for (int ch = 0; ch < (kOp == kOpQkRope ? 0 : BN / 32); ++ch) {
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t ra[32], rb[32];
+          tmem_ld_32(tbase + ch * 32, ra);
+          tmem_ld_32(tbase + 128 + ch * 32, rb);
+          tmem_wait_ld();
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float g[2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int c = ch * 32 + j + i;
+              const float a = epi_value<false>(ra[j + i], s_scale[c], s_bias[c], 0.0f, true);
+              const float b = epi_value<false>(rb[j + i], s_scale[128 + c], s_bias[128 + c], 0.0f, true);
+              g[i] = __fdividef(a, 1.0f + __expf(-a)) * b;
+            }
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(g[0], g[1]);
+            packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            st[lane * 8 + (((ch & 1) * 4 + q) ^ (lane & 7))] =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          if (ch & 1) {
+            __syncwarp();
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+              const int u = it * 32 + lane, rr = u >> 3, cu = u & 7;
+              const int grow = row0 + rr;
+              if (grow < M)
+                *reinterpret_cast<uint4*>(static_cast<uint16_t*>(y_out) + static_cast<int64_t>(grow) * ldy + c0 +
+                                          (ch - 1) * 32 + cu * 8) = st[rr * 8 + (cu ^ (rr & 7))];
+            }
+            __syncwarp();
+          }
+        }
+      }
+#pragma unroll 1
+      for (int ch = 0; ch < (kOp == kOpQkRope || kOp == kOpSwiglu ? 0 : BN / 32); ++ch) {
         float4 xnext[8];
         if (kOp == kOpResidual && res_fast && ch + 1 < BN / 32) {
 #pragma unroll
@@ -657,12 +700,16 @@ cudaError_t launch_gemm_bf16_op(const CUtensorMap& tmap_x, const CUtensorMap& tm
                                 const uint16_t* bias, void* y, int op, const float* gate, int64_t m, int* err,
                                 int sm_count, cudaStream_t stream) {
   const PeerOut none = {};
-  if (op == gemm_bf16::kOpGelu)
+  // op: an sc_epilogue value
+  if (op == SC_EPI_GELU_TANH)
     return gemm_bf16::launch_gemm<false, false, gemm_bf16::kOpGelu>(tmap_x, tmap_w, w, bias, y, m, err, sm_count,
                                                                     stream, none);
-  if (op == gemm_bf16::kOpResidual)
+  if (op == SC_EPI_GATED_RESIDUAL)
     return gemm_bf16::launch_gemm<true, false, gemm_bf16::kOpResidual>(tmap_x, tmap_w, w, bias, y, m, err, sm_count,
                                                                        stream, none, gate);
+  if (op == SC_EPI_SWIGLU)
+    return gemm_bf16::launch_gemm<false, false, gemm_bf16::kOpSwiglu>(tmap_x, tmap_w, w, bias, y, m, err, sm_count,
+                                                                      stream, none);
   return cudaErrorInvalidValue;
 }
 

@@ -131,8 +131,8 @@ cudaError_t launch_gemm_i8(const CUtensorMap& tmap_codes, const CUtensorMap& tma
                            const uint16_t* bias, void* y, bool f32_out, const float* row_scales, int64_t m, int* err,
                            int sm_count, cudaStream_t stream);
 constexpr int64_t kW8A8MaxK = 32768;  // a row held whole in shared memory as fp32 (128 KB)
-// The bf16-operand pair GEMM with a fused epilogue operation: op 1 = GELU (tanh) before the bf16 store,
-// op 2 = y (fp32) += gate[n] * v in place (the gated residual).
+// The bf16-operand pair GEMM with a fused epilogue operation, op an sc_epilogue value: GELU (tanh) before
+// the bf16 store, y (fp32) += gate[n] * v in place (the gated residual), or SwiGLU of gate / up blocks.
 cudaError_t launch_gemm_bf16_op(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
                                 const uint16_t* bias, void* y, int op, const float* gate, int64_t m, int* err,
                                 int sm_count, cudaStream_t stream);

@@ -34,6 +34,21 @@ from .products import Context, QuantizedWeight
 # products before them (sc_linear_epilogue).
 FUSED_EPILOGUES = True
 FUSE_MIN_ROWS = 1536
+# The Z-Image block's gate / up product is registered with its halves in blocks of 128 columns, so that
+# each 256-column tile of the product holds a gate block and its up block (SC_EPI_SWIGLU).
+SWIGLU_BLOCK = 128
+
+
+def interleave_halves(w: torch.Tensor, block: int) -> torch.Tensor:
+    """Rows [gate (h) ; up (h)] of a [2 h, k] weight -> gate block j, up block j, ... (blocks of `block`)."""
+    h = w.shape[0] // 2
+    return torch.stack([w[:h].reshape(h // block, block, -1), w[h:].reshape(h // block, block, -1)], 1).reshape(w.shape)
+
+
+def deinterleave_halves(v: torch.Tensor, block: int) -> torch.Tensor:
+    """Columns of a product of an interleaved weight -> [gate (h) | up (h)]."""
+    rows, n = v.shape
+    return v.reshape(rows, n // (2 * block), 2, block).transpose(1, 2).reshape(rows, n)
 
 
 def quantize_per_channel(w: torch.Tensor):
@@ -47,9 +62,13 @@ class Linear:
     """One int8 per-channel linear [out, in] in the library, from N(0, std) weights (random init)."""
 
     def __init__(self, ctx: Context, n_out: int, k_in: int, gen: torch.Generator, std: float = 0.02,
-                 bias: bool = False):
+                 bias: bool = False, interleave: int = 0):
+        """interleave: a gate / up product [2 h, k] whose halves are registered in blocks of `interleave`
+        columns (gate block j, then up block j), the layout of the SwiGLU epilogue; outputs keep it."""
         dev = f"cuda:{ctx.device}"
         w = torch.randn(n_out, k_in, generator=gen, device=dev) * std
+        if interleave:
+            w = interleave_halves(w, interleave)
         q, s = quantize_per_channel(w)
         del w
         self.weight = QuantizedWeight(ctx, q, abi.WEIGHT_INT8, s, published_nk=True)
@@ -83,6 +102,15 @@ class Linear:
             return
         self(x, scratch, workspace)
         dk.qk_norm_rope(scratch, batch, tokens, q.shape[1], norm_q, norm_k, freqs, eps, q, k, v, q.shape[2], offset)
+
+    def swiglu(self, x: torch.Tensor, out: torch.Tensor, scratch: torch.Tensor, workspace=None) -> torch.Tensor:
+        """out (bf16 [rows, h]) = silu(gate) * up of this interleaved gate / up product: in the product's
+        epilogue from FUSE_MIN_ROWS rows, else the product into `scratch` (bf16 [rows, 2 h]) and
+        sd_swiglu_blocks."""
+        if self._fuse(x.shape[0]):
+            return self.weight.linear_epilogue(x, out, abi.EPI_SWIGLU, bias=self.bias, workspace=workspace)
+        self(x, scratch, workspace)
+        return dk.swiglu_blocks(scratch, out.shape[1], SWIGLU_BLOCK, out)
 
     def gated_residual(self, x: torch.Tensor, resid: torch.Tensor, gate: torch.Tensor, scratch: torch.Tensor,
                        workspace=None) -> torch.Tensor:
@@ -162,7 +190,7 @@ class ZImageBlock:
         self.modulation = Linear(ctx, 4 * dim, adaln, g, bias=True)
         self.qkv = Linear(ctx, 3 * dim, dim, g)
         self.out = Linear(ctx, dim, dim, g)
-        self.w13 = Linear(ctx, 2 * hidden, dim, g)
+        self.w13 = Linear(ctx, 2 * hidden, dim, g, interleave=SWIGLU_BLOCK)
         self.w2 = Linear(ctx, dim, hidden, g)
         ones = lambda n: (1.0 + 0.1 * torch.randn(n, generator=g, device=dev)).float()
         self.norm1, self.norm2, self.ffn_norm1, self.ffn_norm2 = ones(dim), ones(dim), ones(dim), ones(dim)
@@ -213,8 +241,7 @@ class ZImageBlock:
         dk.gated_residual(x, b["y"], gate_msa, True, self.norm2, self.eps)
         # feed-forward
         dk.rms_norm_modulate(x, self.ffn_norm1, scale_mlp, self.eps, b["a"])
-        self.w13(b["a"], b["h"], ws)
-        dk.swiglu(b["h"], self.hidden, b["g"])
+        self.w13.swiglu(b["a"], b["g"], b["h"], ws)
         self.w2(b["g"], b["y"], ws)
         dk.gated_residual(x, b["y"], gate_mlp, True, self.ffn_norm2, self.eps)
         return x

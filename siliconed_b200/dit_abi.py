@@ -22,6 +22,7 @@ SIGNATURES = {
     "sd_qk_norm_rope": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _F, _P, _P, _P, _I, _I, _P]),
     "sd_attention_merge": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "sd_swiglu": (_I, [_P, _I64, _I, _P, _P]),
+    "sd_swiglu_blocks": (_I, [_P, _I64, _I, _I, _P, _P]),
     "sd_gelu_tanh": (_I, [_P, _I64, _P]),
 }
 
@@ -102,6 +103,11 @@ def attention_merge(o, batch, heads, joint_len, token_offset, tokens, out):
 
 def swiglu(h, hidden, out):
     _check(load().sd_swiglu(_ptr(h), h.shape[0], hidden, _ptr(out), _stream()), "sd_swiglu")
+    return out
+
+
+def swiglu_blocks(h, hidden, block, out):
+    _check(load().sd_swiglu_blocks(_ptr(h), h.shape[0], hidden, block, _ptr(out), _stream()), "sd_swiglu_blocks")
     return out
 
 

@@ -238,13 +238,15 @@ class QuantizedWeight:
     def linear_epilogue(self, x, out, op: int, bias=None, gate=None, workspace=None, stream=None):
         """sc_linear_epilogue: v = (x . q) * s + bias with the DiT stage `op` fused into the product's
         epilogue.  EPI_GELU_TANH: out bf16 [M, N] = gelu_tanh(v); EPI_GATED_RESIDUAL: out fp32 [M, N]
-        += gate * v in place (gate fp32 [N]).  M must exceed 128."""
+        += gate * v in place (gate fp32 [N]); EPI_SWIGLU: out bf16 [M, N / 2] = silu(gate) * up with the
+        weight's columns in blocks of 128 (gate, up).  M must exceed 128."""
         if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.shape[1] != self.k:
             raise SiliconedError(abi.INVALID_ARG, f"x must be a CUDA bf16 [M, {self.k}] tensor")
         m = x.shape[0]
-        want = torch.bfloat16 if op == abi.EPI_GELU_TANH else torch.float32
-        if out.dtype != want or tuple(out.shape) != (m, self.n) or not out.is_contiguous():
-            raise SiliconedError(abi.INVALID_ARG, f"out must be a contiguous {want} [{m}, {self.n}] tensor")
+        want = torch.float32 if op == abi.EPI_GATED_RESIDUAL else torch.bfloat16
+        n_out = self.n // 2 if op == abi.EPI_SWIGLU else self.n
+        if out.dtype != want or tuple(out.shape) != (m, n_out) or not out.is_contiguous():
+            raise SiliconedError(abi.INVALID_ARG, f"out must be a contiguous {want} [{m}, {n_out}] tensor")
         if gate is not None and (gate.dtype != torch.float32 or gate.numel() != self.n or not gate.is_contiguous()):
             raise SiliconedError(abi.INVALID_ARG, f"gate must be a contiguous fp32 [{self.n}] tensor")
         if workspace is None:

@@ -181,7 +181,8 @@ def test_zimage_block_matches_fp32_reference():
     y = lin_ref(blk.out, o)
     x_ref = x_ref + torch.tanh(mod[1]) * rms_ref(y, blk.norm2)
     a = bf(rms_ref(x_ref, blk.ffn_norm1) * (1 + mod[2]))
-    h = bf(lin_ref(blk.w13, a))
+    from siliconed_b200.dit import deinterleave_halves, SWIGLU_BLOCK
+    h = deinterleave_halves(bf(lin_ref(blk.w13, a)), SWIGLU_BLOCK)   # the weight is registered interleaved
     gg = bf(h[:, :hidden] / (1 + torch.exp(-h[:, :hidden])) * h[:, hidden:])
     y = lin_ref(blk.w2, gg)
     x_ref = x_ref + torch.tanh(mod[3]) * rms_ref(y, blk.ffn_norm2)
@@ -364,5 +365,42 @@ def test_qk_norm_rope_in_the_product_epilogue():
         a, b = a.float(), b.float()
         assert rel(a, b) <= 5e-3, rel(a, b)
         assert float((a - b).abs().max()) <= 0.02 * float(b.abs().max())
+    lin.close()
+    ctx.close()
+
+
+@gpu
+@needs_cuda
+def test_swiglu_in_the_product_epilogue():
+    """From 1536 rows the interleaved gate / up product applies SwiGLU in its epilogue (SC_EPI_SWIGLU):
+    against the product's fp32 output v through silu(a) * b in fp64, within one bf16 rounding plus 2^-10
+    of it for the epilogue's exp-and-divide form; against the separate pass (the product rounded to bf16,
+    then sd_swiglu_blocks) within relative L2 5e-3."""
+    import siliconed_b200.dit as dit
+    from siliconed_b200.products import Context
+    ctx = Context(0)
+    g = torch.Generator(device="cuda").manual_seed(21)
+    hidden, k, rows = 512, 384, 2048
+    lin = dit.Linear(ctx, 2 * hidden, k, g, interleave=dit.SWIGLU_BLOCK)
+    x = torch.randn(rows, k, generator=g, device="cuda").to(torch.bfloat16)
+    ws = torch.empty(lin.workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    scratch = torch.empty(rows, 2 * hidden, dtype=torch.bfloat16, device="cuda")
+    v = dit.deinterleave_halves(lin(x, torch.empty(rows, 2 * hidden, device="cuda"), ws), dit.SWIGLU_BLOCK)
+    outs = {}
+    try:
+        for fused in (True, False):
+            dit.FUSED_EPILOGUES = fused
+            out = torch.empty(rows, hidden, dtype=torch.bfloat16, device="cuda")
+            lin.swiglu(x, out, scratch, ws)
+            outs[fused] = out.float()
+    finally:
+        dit.FUSED_EPILOGUES = True
+    torch.cuda.synchronize()
+    ctx.poll_errors()
+    a, b = v[:, :hidden].double(), v[:, hidden:].double()
+    ref = a / (1 + torch.exp(-a)) * b
+    bound = 2.0 ** -8 * (1 + 2.0 ** -10) * ref.abs() + (a.abs() * b.abs()) * 2.0 ** -20 + 1e-30
+    assert float((outs[True].double() - ref).abs().sub(bound).max()) <= 0.0
+    assert rel(outs[True], outs[False]) <= 5e-3
     lin.close()
     ctx.close()
