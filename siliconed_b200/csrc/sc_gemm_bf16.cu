@@ -583,13 +583,8 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
                         const float* gate = nullptr, const float* row_scales = nullptr, const HeadOut* heads = nullptr) {
   const HeadOut ho = heads != nullptr ? *heads : HeadOut{};
   auto kernel = gemm_bf16_pair<kF32Out, kPeers, kOp, kI8>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static unsigned long long configured = 0;  // per template instance and device
+  if (cudaError_t e = set_smem_once(kernel, static_cast<int>(kSmemBytes), configured); e != cudaSuccess) return e;
   const int m_tiles = static_cast<int>((m + 2 * BM - 1) / (2 * BM));
   const int n_tiles = static_cast<int>(w->n_pad / BN);
   // kI8: 128 codes per stage; the weight's K padding is a multiple of 64, and a last stage past it

@@ -269,12 +269,8 @@ template <int kKind, bool kNaN, bool kF32Out, int MT>
 cudaError_t launch_mt(const CUtensorMap& tm_x, const sc_weight* w, const uint16_t* bias, void* y, int64_t m, int* err,
                       int sm_count, cudaStream_t stream) {
   auto kernel = gemm_w8_skinny<kKind, kNaN, kF32Out, MT>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static unsigned long long configured = 0;  // per template instance and device
+  if (cudaError_t e = set_smem_once(kernel, static_cast<int>(kSmemBytes), configured); e != cudaSuccess) return e;
   const int n_tiles = static_cast<int>(w->n_pad / BN);
   const int k_tiles = static_cast<int>(w->k_pad / BK);
   int ks = 1;

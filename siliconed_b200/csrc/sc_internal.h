@@ -12,6 +12,20 @@
 // The weight arena's geometry: every weight is stored transposed, [n_pad][k_pad] bytes, K padded
 // to the GEMM's K tile and N to its N tile, so that no TMA box ever leaves the arena.
 namespace sc {
+// cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) once per device: the attribute belongs to
+// the function in the current device's context, so a process that drives several GPUs sets it on each.
+template <typename Kernel>
+inline cudaError_t set_smem_once(Kernel kernel, int bytes, unsigned long long& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done |= bit;
+  return e;
+}
+
 constexpr int kArenaKAlign = 64;    // the GEMM's BK (one 128-byte swizzle row of bf16)
 constexpr int kArenaNAlign = 256;   // the GEMM's BN
 constexpr int kErrWords = 4;        // device error word: code, site, block, spare

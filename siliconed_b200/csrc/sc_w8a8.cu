@@ -105,14 +105,11 @@ cudaError_t launch_quantize_rows(const void* x, bool x_f32, int64_t m, int64_t k
                                  float* scales, cudaStream_t stream) {
   if (m > 0x7FFFFFFF || k > kW8A8MaxK) return cudaErrorInvalidValue;
   const int smem = static_cast<int>((k + 255) / 256 * 256 * 4);
-  static bool configured[2] = {false, false};
-  if (!configured[x_f32]) {
-    cudaError_t e = cudaFuncSetAttribute(x_f32 ? quantize_rows<true> : quantize_rows<false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kW8A8MaxK * 4));
-    if (e != cudaSuccess) return e;
-    configured[x_f32] = true;
-  }
+  static unsigned long long configured[2] = {0, 0};  // per input type and device
+  if (cudaError_t e = set_smem_once(x_f32 ? quantize_rows<true> : quantize_rows<false>, static_cast<int>(kW8A8MaxK * 4),
+                                    configured[x_f32]);
+      e != cudaSuccess)
+    return e;
   if (x_f32)
     quantize_rows<true><<<static_cast<unsigned>(m), kQThreads, smem, stream>>>(x, k, group, codes, ld, scales);
   else
