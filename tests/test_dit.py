@@ -404,3 +404,14 @@ def test_swiglu_in_the_product_epilogue():
     assert rel(outs[True], outs[False]) <= 5e-3
     lin.close()
     ctx.close()
+
+
+def test_interleave_halves_round_trip():
+    """The gate / up weight's interleaved registration and the product columns' inverse (CPU)."""
+    from siliconed_b200.dit import interleave_halves, deinterleave_halves
+    w = torch.randn(2 * 384, 40)
+    wi = interleave_halves(w, 128)
+    assert torch.equal(wi[:128], w[:128]) and torch.equal(wi[128:256], w[384:512])
+    assert torch.equal(wi[256:384], w[128:256])
+    x = torch.randn(7, 40, dtype=torch.float64)
+    assert torch.allclose(deinterleave_halves(x @ wi.double().T, 128), x @ w.double().T)
