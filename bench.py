@@ -281,13 +281,18 @@ def run_ours(args):
     y_host = torch.empty((case.m, case.n), dtype=torch.bfloat16).pin_memory()
     x_dev = torch.empty_like(x)
     e2e_steps = max(3, min(args.steps, 20))
+    # y goes through a device buffer and chunked copies back (the products writing the pinned y themselves,
+    # sc_linear_host's direct mode, measured slower: 97 against 104 TFLOP/s end to end for config 1).
+    direct_out = False
+
     def e2e_step():
         if w8a8:   # copy in, product, copy out on one stream
             x_dev.copy_(x_host, non_blocking=True)
             w.linear_w8a8(x_dev, y, bias=bias, workspace=ws, stream=stream)
             y_host.copy_(y, non_blocking=True)
         else:
-            w.linear_host(x_host, y_host, bias=bias, x_dev=x_dev, y_dev=y, workspace=ws, stream=stream)
+            w.linear_host(x_host, y_host, bias=bias, x_dev=x_dev, y_dev=None if direct_out else y, workspace=ws,
+                          stream=stream, direct=direct_out)
     for _ in range(2):
         e2e_step()
     if world > 1:
@@ -337,7 +342,9 @@ def run_ours(args):
                         "h2d_bytes_per_step": int(case.x.nbytes),
                         "d2h_bytes_per_step": int(case.m * case.n * 2),
                         "path": "QuantizedWeight.linear_host (sc_linear_host): pinned host x in, y out, every step; "
-                                "copies overlapped with the products in chunks of rows"},
+                                "x copied in chunks of rows overlapped with the products"
+                                + ("; the products write the pinned y themselves" if direct_out else
+                                   "; y copied back in chunks")},
                 "gpu_launches": args.steps * (3 if w8a8 else len(route_kernels(case, ws_bytes))),
                 "step_ms_min": min(per_step), "step_ms_median": statistics.median(per_step)}
         if w8a8:

@@ -228,6 +228,8 @@ SC_API sc_status sc_linear_epilogue(sc_ctx* ctx, const sc_weight* w, const sc_bf
  * `stream`: y_host is complete when `stream` reaches the call's end; x_host and y_host must be page-locked
  * for the copies to overlap.  No counterpart in the reference, where the GPU reads the host's memory
  * (Apple silicon's unified memory: the MTLBuffers of WeightProducts.linear are wrapped no-copy).
+ * y_dev NULL: the products write y_host themselves (page-locked host memory the GPU can address; needs the
+ * widened route's workspace and no rotation), eight chunks by default, nothing copied back.
  */
 SC_API sc_status sc_linear_host(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x_host, int64_t m, const sc_bf16* bias,
                                 void* y_host, sc_out_type y_type, sc_bf16* x_dev, void* y_dev, void* workspace,

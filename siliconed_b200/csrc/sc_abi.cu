@@ -602,8 +602,25 @@ sc_status sc_linear_host(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x_host,
   if (m < 0 || chunk_rows < 0) return fail(ctx, SC_INVALID_ARG, "m < 0 or chunk_rows < 0");
   if (m == 0) return SC_OK;
   if (x_host == nullptr || y_host == nullptr) return fail(ctx, SC_INVALID_ARG, "null host buffer");
-  sc_status s = check_product_args(ctx, w, x_dev, m, bias, y_dev);
+  // y_dev NULL: the products write y_host themselves (page-locked host memory the GPU can address), so
+  // no copy back is queued and the output crosses PCIe while the tiles are computed.
+  const bool direct_out = y_dev == nullptr;
+  void* y_out = y_dev;
+  if (direct_out) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, y_host) != cudaSuccess || a.type != cudaMemoryTypeHost || a.devicePointer == nullptr) {
+      cudaGetLastError();
+      return fail(ctx, SC_INVALID_ARG, "y_dev NULL needs a page-locked y_host the GPU can address");
+    }
+    y_out = a.devicePointer;
+    if (w->rotation != 0 || workspace == nullptr || workspace_bytes < widened_bytes(w) ||
+        (reinterpret_cast<uintptr_t>(workspace) & 255u))
+      return fail(ctx, SC_WORKSPACE_TOO_SMALL,
+                  "y_dev NULL needs the widened route: a 256-byte aligned workspace of n_pad * k_pad * 2 bytes");
+  }
+  sc_status s = check_product_args(ctx, w, x_dev, m, bias, direct_out ? static_cast<void*>(x_dev) : y_dev);
   if (s != SC_OK) return s;
+  if ((reinterpret_cast<uintptr_t>(y_out) & 15u)) return fail(ctx, SC_UNALIGNED, "y must be 16-byte aligned");
   if ((s = enter(ctx)) != SC_OK) return s;
   if (ctx->copy_in == nullptr) {
     if ((s = check_cuda(ctx, cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking), "copy stream")) != SC_OK ||
@@ -618,7 +635,8 @@ sc_status sc_linear_host(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x_host,
   // The default: four chunks.  On B200 over PCIe, chunks of 1024 rows of config 1 (6.3 MB each way) took
   // 0.75 ms a step against 0.99 ms unchunked and 0.84 ms with eight chunks (each copy and each cross-stream
   // wait costs a few tens of microseconds; both directions at once move 50 MB in 0.51 ms at best).
-  int64_t chunk = chunk_rows > 0 ? chunk_rows : (m + 3) / 4;
+  // Writing y directly (no copy back), eight chunks: each chunk's product overlaps the next chunk's copy in.
+  int64_t chunk = chunk_rows > 0 ? chunk_rows : (direct_out ? (m + 7) / 8 : (m + 3) / 4);
   chunk = (chunk + 255) / 256 * 256;
   if (chunk < 512) chunk = 512;
   if ((m + chunk - 1) / chunk > kHostMaxChunks) chunk = ((m + kHostMaxChunks - 1) / kHostMaxChunks + 255) / 256 * 256;
@@ -650,7 +668,7 @@ sc_status sc_linear_host(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x_host,
   // With room for the widened weight (and no rotation to stage), the codes are widened once, while the
   // first chunk arrives, and every chunk runs the bf16-operand pair GEMM on them: the widened route's
   // bits, without widening per chunk.  Otherwise each chunk is an ordinary product.
-  const bool widen_once = chunks > 1 && w->rotation == 0 && workspace != nullptr &&
+  const bool widen_once = (chunks > 1 || direct_out) && w->rotation == 0 && workspace != nullptr &&
                           workspace_bytes >= widened_bytes(w) && (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0;
   CUtensorMap tmw;
   if (widen_once) {
@@ -660,7 +678,7 @@ sc_status sc_linear_host(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x_host,
   for (int c = 0; c < chunks; ++c) {
     const int64_t r0 = starts[c], rows = starts[c + 1] - starts[c];
     if ((s = check_cuda(ctx, cudaStreamWaitEvent(st, ev_in[c], 0), "stream wait")) != SC_OK) return s;
-    void* yc = static_cast<uint8_t*>(y_dev) + static_cast<size_t>(r0 * w->n) * ysz;
+    void* yc = static_cast<uint8_t*>(y_out) + static_cast<size_t>(r0 * w->n) * ysz;
     if (widen_once) {
       CUtensorMap tmx;
       if ((s = make_tmap_x(ctx, x_dev + r0 * w->k, rows, w->k, &tmx)) != SC_OK) return s;
@@ -672,6 +690,7 @@ sc_status sc_linear_host(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x_host,
                                workspace_bytes, stream, 0)) != SC_OK) {
       return s;
     }
+    if (direct_out) continue;
     if ((s = check_cuda(ctx, cudaEventRecord(ev_out[c], st), "event record")) != SC_OK ||
         (s = check_cuda(ctx, cudaStreamWaitEvent(ctx->copy_out, ev_out[c], 0), "stream wait")) != SC_OK ||
         (s = check_cuda(ctx, cudaMemcpyAsync(static_cast<uint8_t*>(y_host) + static_cast<size_t>(r0 * w->n) * ysz, yc,
@@ -680,6 +699,7 @@ sc_status sc_linear_host(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x_host,
                         "copy out")) != SC_OK)
       return s;
   }
+  if (direct_out) return SC_OK;  // the products on `stream` wrote y_host themselves
   // The caller's stream holds until the last copy out is done.
   if ((s = check_cuda(ctx, cudaEventRecord(ev_end, ctx->copy_out), "event record")) != SC_OK) return s;
   return check_cuda(ctx, cudaStreamWaitEvent(st, ev_end, 0), "stream wait");

@@ -257,10 +257,11 @@ class QuantizedWeight:
         return out
 
     def linear_host(self, x_host, out_host, bias=None, x_dev=None, y_dev=None, workspace=None, chunk_rows: int = 0,
-                    stream=None):
+                    stream=None, direct: bool = False):
         """sc_linear_host: out_host (CPU, bf16 or fp32 [M, N]) = x_host (CPU bf16 [M, K]) . W + bias, the copies
         overlapped with the products in chunks of rows.  Pinned host tensors let the copies overlap; x_dev /
-        y_dev are device staging buffers (allocated here when not given)."""
+        y_dev are device staging buffers (allocated here when not given).  direct: the products write the
+        pinned out_host themselves (no y_dev, no copy back)."""
         if x_host.dtype != torch.bfloat16 or x_host.is_cuda or x_host.dim() != 2 or x_host.shape[1] != self.k:
             raise SiliconedError(abi.INVALID_ARG, f"x_host must be a CPU bf16 [M, {self.k}] tensor")
         m = x_host.shape[0]
@@ -270,9 +271,11 @@ class QuantizedWeight:
         dev = f"cuda:{self.ctx.device}"
         if x_dev is None:
             x_dev = torch.empty((m, self.k), dtype=torch.bfloat16, device=dev)
-        if y_dev is None:
+        if direct:
+            y_dev = None
+        elif y_dev is None:
             y_dev = torch.empty((m, self.n), dtype=out_host.dtype, device=dev)
-        need = self.workspace_bytes(m)
+        need = self.epilogue_workspace_bytes(m) if direct else self.workspace_bytes(m)
         if need and workspace is None:
             workspace = self.ctx.workspace(need, dev)
         ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()

@@ -584,9 +584,10 @@ def test_fused_epilogue_guards(ctx):
 # sc_linear_host: host buffers, copies overlapped with the products in chunks of rows
 
 
-@pytest.mark.parametrize("m,chunk", [(4096, 0), (4096, 1024), (1000, 0), (700, 512), (600, 0), (3, 0), (40, 0),
-                                     (2000, 256)])
-def test_linear_host_has_the_device_bits(ctx, m, chunk):
+@pytest.mark.parametrize("m,chunk,direct", [(4096, 0, False), (4096, 1024, False), (1000, 0, False), (700, 512, False),
+                                            (600, 0, False), (3, 0, False), (40, 0, False), (2000, 256, False),
+                                            (4096, 0, True), (1000, 0, True), (200, 0, True), (2000, 256, True)])
+def test_linear_host_has_the_device_bits(ctx, m, chunk, direct):
     """Chunked copies and products give each row the bits of the whole batch's device product."""
     g = np.random.default_rng(m + chunk)
     k, n = 768, 1280
@@ -600,10 +601,10 @@ def test_linear_host_has_the_device_bits(ctx, m, chunk):
         want = linear_ex(ctx, w, bf16_dev(x), m, bd, f32, workspace=True)
         out = torch.empty((m, n), dtype=torch.float32 if f32 else torch.bfloat16).pin_memory()
         out.fill_(float("nan"))
-        w.linear_host(x_host, out, bias=bd, chunk_rows=chunk)
+        w.linear_host(x_host, out, bias=bd, chunk_rows=chunk, direct=direct)
         torch.cuda.synchronize()
         ctx.poll_errors()
         a = want.cpu().view(torch.int32 if f32 else torch.int16).numpy()
         b = out.view(torch.int32 if f32 else torch.int16).numpy()
-        assert np.array_equal(a, b), f"m {m}, chunk {chunk}, f32 {f32}: {int(np.sum(a != b))} differ"
+        assert np.array_equal(a, b), f"m {m}, chunk {chunk}, direct {direct}, f32 {f32}: {int(np.sum(a != b))} differ"
     w.close()
