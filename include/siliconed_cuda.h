@@ -251,6 +251,19 @@ SC_API sc_status sc_linear_qk_norm_rope(sc_ctx* ctx, const sc_weight* w, const s
                                         const float* norm_k, const float* freqs, float eps, void* workspace,
                                         size_t workspace_bytes, void* stream);
 
+/*
+ * The product whose operand is the attention's output o [batch, heads, joint, 128] bf16 itself: row r of the
+ * operand is token r % tokens of image r / tokens, at position offset + r % tokens, its K = heads * 128
+ * values head after head (the rows a merge pass would gather; no counterpart in the reference, whose
+ * attention writes the merged rows).  y [batch * tokens, n]: bf16 or fp32 (y_type) with op 0, or with op
+ * SC_EPI_GATED_RESIDUAL the fp32 residual stream += gate[n] * v in place.  tokens a multiple of 128; the
+ * workspace of sc_linear_epilogue; not for a convrot weight.
+ */
+SC_API sc_status sc_linear_heads(sc_ctx* ctx, const sc_weight* w, const sc_bf16* o, int64_t batch, int heads,
+                                 int64_t joint, int64_t offset, int64_t tokens, const sc_bf16* bias, void* y,
+                                 sc_out_type y_type, sc_epilogue op, const float* gate, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* sc_linear_ex with its scratch in a 32 MiB device array of the library instead of a workspace: it
  * allocates nothing and takes no workspace argument.  No counterpart in the reference: it serves
  * callers that have no scratch buffer to pass (a binding that keeps the signature of

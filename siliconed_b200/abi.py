@@ -49,6 +49,7 @@ SIGNATURES = {
     "sc_linear_ex": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _SZ, _P]),
     "sc_linear_epilogue": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _P, _SZ, _P]),
     "sc_weight_set_rotation": (_I, [_P, _P, _I]),
+    "sc_linear_heads": (_I, [_P, _P, _P, _I64, _I, _I64, _I64, _I64, _P, _P, _I, _I, _P, _P, _SZ, _P]),
     "sc_linear_qk_norm_rope": (_I, [_P, _P, _P, _I64, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P, _P, _P,
                                     ctypes.c_float, _P, _SZ, _P]),
     "sc_linear_host": (_I, [_P, _P, _P, _I64, _P, _P, _I, _P, _P, _P, _SZ, _I64, _P]),

@@ -129,6 +129,21 @@ sc_status make_tmap_codes(sc_ctx* ctx, const void* base, int64_t inner, int64_t 
 }
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+// Map over the attention's output o [batch, heads, joint, 128] bf16 as the product's operand: box 64 values
+// x 128 tokens of one head of one image, 128-byte swizzle (the same shared-memory tile as make_tmap_x's).
+sc_status make_tmap_heads(sc_ctx* ctx, const sc_bf16* o, int64_t batch, int64_t heads, int64_t joint, CUtensorMap* map) {
+  const cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(joint), static_cast<cuuint64_t>(heads),
+                              static_cast<cuuint64_t>(batch)};
+  const cuuint64_t strides[3] = {256, static_cast<cuuint64_t>(joint) * 256, static_cast<cuuint64_t>(heads * joint) * 256};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = ctx->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<sc_bf16*>(o), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, SC_CUDA_ERROR, "cuTensorMapEncodeTiled (attention output) failed: " + std::to_string(r));
+  return SC_OK;
+}
 int64_t w8a8_ld(int64_t k) { return (k + 15) / 16 * 16; }
 size_t w8a8_workspace(const sc_weight* w, int64_t m) {
   return align256(signed_codes_bytes(w)) + align256(static_cast<size_t>(m * w8a8_ld(w->k))) +
@@ -749,6 +764,44 @@ sc_status sc_linear_qk_norm_rope(sc_ctx* ctx, const sc_weight* w, const sc_bf16*
   ho.offset = static_cast<int>(offset);
   return check_cuda(ctx, launch_gemm_bf16_heads(tmx, tmw, w, bias, ho, m, ctx->d_err, ctx->sm_count, st),
                     "qk-norm gemm launch");
+}
+
+sc_status sc_linear_heads(sc_ctx* ctx, const sc_weight* w, const sc_bf16* o, int64_t batch, int heads, int64_t joint,
+                          int64_t offset, int64_t tokens, const sc_bf16* bias, void* y, sc_out_type y_type,
+                          sc_epilogue op, const float* gate, void* workspace, size_t workspace_bytes, void* stream) {
+  if (ctx == nullptr) return SC_INVALID_ARG;
+  if (w == nullptr || o == nullptr || y == nullptr) return fail(ctx, SC_INVALID_ARG, "null weight, o or y");
+  if (y_type != SC_OUT_BF16 && y_type != SC_OUT_F32) return fail(ctx, SC_INVALID_ARG, "unknown output type");
+  if (op != 0 && op != SC_EPI_GATED_RESIDUAL) return fail(ctx, SC_INVALID_ARG, "epilogue: none or the gated residual");
+  if (op == SC_EPI_GATED_RESIDUAL && (y_type != SC_OUT_F32 || gate == nullptr || !is_device_pointer(gate) ||
+                                      (reinterpret_cast<uintptr_t>(gate) & 3u)))
+    return fail(ctx, SC_INVALID_ARG, "the gated residual needs an fp32 y and a 4-byte aligned device gate");
+  if (batch < 1 || heads < 1 || tokens < 1 || offset < 0 || offset + tokens > joint || joint > 0x7FFFFFFF)
+    return fail(ctx, SC_INVALID_ARG, "batch, heads, tokens >= 1 and offset + tokens <= joint");
+  if (tokens % 128 != 0) return fail(ctx, SC_UNSUPPORTED_SHAPE, "tokens must be a multiple of 128");
+  if (w->k != 128LL * heads) return fail(ctx, SC_UNSUPPORTED_SHAPE, "K must be heads * 128");
+  if (w->rotation != 0) return fail(ctx, SC_UNSUPPORTED_SHAPE, "a convrot weight takes its operand through sc_linear");
+  if (w->device != ctx->device) return fail(ctx, SC_INVALID_ARG, "weight registered on another device");
+  const int64_t m = batch * tokens;
+  if (m <= kPairMinRows || m > 0x7FFFFFFF) return fail(ctx, SC_UNSUPPORTED_SHAPE, "sc_linear_heads takes more than 128 rows");
+  if ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(y)) & 15u ||
+      (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 1u)))
+    return fail(ctx, SC_UNALIGNED, "o and y must be 16-byte aligned, bias 2-byte aligned");
+  if (!is_device_pointer(o) || !is_device_pointer(y) || (bias != nullptr && !is_device_pointer(bias)))
+    return fail(ctx, SC_INVALID_ARG, "o, y and bias must be device memory");
+  if (workspace == nullptr || workspace_bytes < widened_bytes(w) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(ctx, SC_WORKSPACE_TOO_SMALL, "sc_linear_heads needs a 256-byte aligned workspace of n_pad * k_pad * 2 bytes");
+  sc_status s = enter(ctx);
+  if (s != SC_OK) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap tmo, tmw;
+  if ((s = make_tmap_heads(ctx, o, batch, heads, joint, &tmo)) != SC_OK) return s;
+  if ((s = make_tmap_widened(ctx, w, workspace, &tmw)) != SC_OK) return s;
+  if ((s = check_cuda(ctx, launch_widen(w, workspace, ctx->sm_count, st), "widen launch")) != SC_OK) return s;
+  const XHeads xh = {static_cast<int>(tokens), static_cast<int>(offset)};
+  return check_cuda(ctx, launch_gemm_bf16_xheads(tmo, tmw, w, bias, y, y_type == SC_OUT_F32, static_cast<int>(op), gate,
+                                                 xh, m, ctx->d_err, ctx->sm_count, st),
+                    "heads gemm launch");
 }
 
 sc_status sc_linear_epilogue(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias,

@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const float* __restrict__ scales, const uint16_t* __restrict__ bias, void* __restrict__ y_out,
                    int M, int N, int k_tiles, int m_tiles, int n_tiles, int* err,
                    const __grid_constant__ PeerOut peers, const float* __restrict__ gate,
-                   const float* __restrict__ row_scales, const __grid_constant__ HeadOut ho) {
+                   const float* __restrict__ row_scales, const __grid_constant__ HeadOut ho, const XHeads xh) {
   static_assert(kOp != kOpResidual || kF32Out, "the residual is fp32");
   static_assert(kOp != kOpGelu || !kF32Out, "the GELU output is bf16");
   static_assert(!kI8 || (kOp == kOpNone && !kPeers), "W8A8 stores plain outputs");
@@ -159,7 +159,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort, err, kSiteProducerEmpty)) break;
           if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (kABytes + kBBytes));
           const uint32_t bar = peer_addr(&s.full[stage], 0);
-          tma_load_2d_pair(s.a[stage], &tm_x, bar, kt * kBKElems, row0);
+          if (xh.tokens > 0)  // 64 values of head kt / 2 for 128 tokens of one image (row0 % 128 == 0)
+            tma_load_4d_pair(s.a[stage], &tm_x, bar, (kt & 1) * 64, xh.offset + row0 % xh.tokens, kt >> 1,
+                             row0 / xh.tokens);
+          else
+            tma_load_2d_pair(s.a[stage], &tm_x, bar, kt * kBKElems, row0);
           tma_load_2d_pair(s.b[stage], &tm_w, bar, kt * kBKElems, col0);
           issued |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
@@ -580,8 +584,10 @@ __global__ void __launch_bounds__(256) widen_codes(const uint4* __restrict__ cod
 template <bool kF32Out, bool kPeers, int kOp = kOpNone, bool kI8 = false>
 cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const sc_weight* w, const uint16_t* bias,
                         void* y, int64_t m, int* err, int sm_count, cudaStream_t stream, const PeerOut& peers,
-                        const float* gate = nullptr, const float* row_scales = nullptr, const HeadOut* heads = nullptr) {
+                        const float* gate = nullptr, const float* row_scales = nullptr, const HeadOut* heads = nullptr,
+                        const XHeads* x_heads = nullptr) {
   const HeadOut ho = heads != nullptr ? *heads : HeadOut{};
+  const XHeads xh = x_heads != nullptr ? *x_heads : XHeads{0, 0};
   auto kernel = gemm_bf16_pair<kF32Out, kPeers, kOp, kI8>;
   static unsigned long long configured = 0;  // per template instance and device
   if (cudaError_t e = set_smem_once(kernel, static_cast<int>(kSmemBytes), configured); e != cudaSuccess) return e;
@@ -611,7 +617,7 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias, y,
                             static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers, gate,
-                            row_scales, ho);
+                            row_scales, ho, xh);
 }
 
 // The weight's arena codes (int8 stored biased by 128) made signed again for the int8 MMA: code ^ 0x80.
@@ -675,6 +681,21 @@ cudaError_t launch_gemm_bf16(const CUtensorMap& tmap_x, const CUtensorMap& tmap_
   const PeerOut none = {};
   return f32_out ? gemm_bf16::launch_gemm<true, false>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream, none)
                  : gemm_bf16::launch_gemm<false, false>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream, none);
+}
+
+cudaError_t launch_gemm_bf16_xheads(const CUtensorMap& tmap_o, const CUtensorMap& tmap_w, const sc_weight* w,
+                                    const uint16_t* bias, void* y, bool f32_out, int op, const float* gate,
+                                    const XHeads& xh, int64_t m, int* err, int sm_count, cudaStream_t stream) {
+  const PeerOut none = {};
+  using namespace gemm_bf16;
+  if (op == SC_EPI_GATED_RESIDUAL)
+    return launch_gemm<true, false, kOpResidual>(tmap_o, tmap_w, w, bias, y, m, err, sm_count, stream, none, gate,
+                                                 nullptr, nullptr, &xh);
+  if (op != 0) return cudaErrorInvalidValue;
+  return f32_out ? launch_gemm<true, false>(tmap_o, tmap_w, w, bias, y, m, err, sm_count, stream, none, nullptr,
+                                            nullptr, nullptr, &xh)
+                 : launch_gemm<false, false>(tmap_o, tmap_w, w, bias, y, m, err, sm_count, stream, none, nullptr,
+                                             nullptr, nullptr, &xh);
 }
 
 cudaError_t launch_gemm_bf16_heads(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,

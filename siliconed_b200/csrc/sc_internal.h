@@ -128,6 +128,15 @@ struct HeadOut {
   float eps;
   int heads, tokens, joint, offset;
 };
+// x given as the attention's output o [batch, heads, joint, 128] (a 4-D tensor map): the product's row r is
+// token r % tokens of image r / tokens at position offset + r % tokens, K = heads * 128.  tokens 0: x is a
+// plain [M, K] matrix.
+struct XHeads {
+  int tokens, offset;
+};
+cudaError_t launch_gemm_bf16_xheads(const CUtensorMap& tmap_o, const CUtensorMap& tmap_w, const sc_weight* w,
+                                    const uint16_t* bias, void* y, bool f32_out, int op, const float* gate,
+                                    const XHeads& xh, int64_t m, int* err, int sm_count, cudaStream_t stream);
 cudaError_t launch_gemm_bf16_heads(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
                                    const uint16_t* bias, const HeadOut& heads, int64_t m, int* err, int sm_count,
                                    cudaStream_t stream);

@@ -112,6 +112,29 @@ class Linear:
         self(x, scratch, workspace)
         return dk.swiglu_blocks(scratch, out.shape[1], SWIGLU_BLOCK, out)
 
+    def _reads_heads(self, o: torch.Tensor, n: int) -> bool:
+        return self._fuse(o.shape[0] * n) and o.is_contiguous() and n % 128 == 0
+
+    def from_heads(self, o: torch.Tensor, off: int, n: int, out: torch.Tensor, merged: torch.Tensor,
+                   workspace=None) -> torch.Tensor:
+        """out = (rows of the attention's output o [B, H, J, 128] at positions off .. off + n) W^T + b: the
+        product reads o itself from FUSE_MIN_ROWS rows (sc_linear_heads), else the rows are merged into
+        `merged` first."""
+        if self._reads_heads(o, n):
+            return self.weight.linear_heads(o, n, off, out, bias=self.bias, workspace=workspace)
+        rows = merged_rows(o, o.shape[0], o.shape[1], o.shape[2], off, n, merged)
+        return self(rows, out, workspace)
+
+    def gated_residual_heads(self, o: torch.Tensor, off: int, n: int, resid: torch.Tensor, gate: torch.Tensor,
+                             merged: torch.Tensor, scratch: torch.Tensor, workspace=None) -> torch.Tensor:
+        """resid (fp32) += gate * (rows of o) W^T: the product reading o itself with the gated residual in its
+        epilogue from FUSE_MIN_ROWS rows, else merge, product and sd_gated_residual."""
+        if self._reads_heads(o, n):
+            return self.weight.linear_heads(o, n, off, resid, bias=self.bias, op=abi.EPI_GATED_RESIDUAL, gate=gate,
+                                            workspace=workspace)
+        rows = merged_rows(o, o.shape[0], o.shape[1], o.shape[2], off, n, merged)
+        return self.gated_residual(rows, resid, gate, scratch, workspace)
+
     def gated_residual(self, x: torch.Tensor, resid: torch.Tensor, gate: torch.Tensor, scratch: torch.Tensor,
                        workspace=None) -> torch.Tensor:
         """resid (fp32) += gate * (x W^T + b): fused into the product's epilogue from FUSE_MIN_ROWS rows,
@@ -236,8 +259,7 @@ class ZImageBlock:
         self.qkv.qkv_heads(b["a"], b["q"], b["k"], b["v"], self.norm_q, self.norm_k, freqs, self.eps, 1, s, 0, b["qkv"],
                            ws)
         o = attention(b["q"], b["k"], b["v"])
-        merged = merged_rows(o, 1, self.heads, s, 0, s, b["merged"])
-        self.out(merged, b["y"], ws)
+        self.out.from_heads(o, 0, s, b["y"], b["merged"], ws)
         dk.gated_residual(x, b["y"], gate_msa, True, self.norm2, self.eps)
         # feed-forward
         dk.rms_norm_modulate(x, self.ffn_norm1, scale_mlp, self.eps, b["a"])
@@ -301,8 +323,7 @@ class MMDiTBlock:
         for (sw, x, n, off), m in zip(streams, mods):
             rows = x.shape[0]
             y, a, h = b["y"][:rows], b["a"][:rows], b["h"][:rows]
-            merged = merged_rows(o, batch, H, joint, off, n, b["merged"][:rows])
-            sw.out.gated_residual(merged, x, m[2], y, ws)
+            sw.out.gated_residual_heads(o, off, n, x, m[2], b["merged"][:rows], y, ws)
             dk.layer_norm_modulate(x, m[4], m[3], self.eps, a)
             sw.mlp1.gelu(a, h, ws)
             sw.mlp2.gated_residual(h, x, m[5], y, ws)

@@ -235,6 +235,26 @@ class QuantizedWeight:
             _stream_ptr(stream)))
         return q, k, v
 
+    def linear_heads(self, o, tokens: int, offset: int, out, bias=None, op: int = 0, gate=None, workspace=None,
+                     stream=None):
+        """sc_linear_heads: the product of the attention's output o (bf16 [B, H, J, 128], contiguous) read as
+        the rows of [B * tokens, H * 128] (positions offset ...), into out (bf16 or fp32 [B * tokens, N]; with
+        op EPI_GATED_RESIDUAL the fp32 residual += gate * v)."""
+        if o.dtype != torch.bfloat16 or not o.is_cuda or o.dim() != 4 or o.shape[3] != 128 or not o.is_contiguous():
+            raise SiliconedError(abi.INVALID_ARG, "o must be a contiguous CUDA bf16 [B, H, J, 128] tensor")
+        batch, heads, joint = o.shape[0], o.shape[1], o.shape[2]
+        m = batch * tokens
+        if out.dtype not in (torch.bfloat16, torch.float32) or tuple(out.shape) != (m, self.n) or not out.is_contiguous():
+            raise SiliconedError(abi.INVALID_ARG, f"out must be a contiguous bf16 or fp32 [{m}, {self.n}] tensor")
+        if workspace is None:
+            workspace = self.ctx.workspace(self.epilogue_workspace_bytes(m), o.device)
+        ws_bytes = workspace.numel() * workspace.element_size()
+        y_type = abi.OUT_F32 if out.dtype == torch.float32 else abi.OUT_BF16
+        self.ctx.check(self.ctx.lib.sc_linear_heads(self.ctx.ptr, self.ptr, _ptr(o), batch, heads, joint, int(offset),
+                                                    int(tokens), _ptr(bias), _ptr(out), y_type, int(op), _ptr(gate),
+                                                    _ptr(workspace), ws_bytes, _stream_ptr(stream)))
+        return out
+
     def linear_epilogue(self, x, out, op: int, bias=None, gate=None, workspace=None, stream=None):
         """sc_linear_epilogue: v = (x . q) * s + bias with the DiT stage `op` fused into the product's
         epilogue.  EPI_GELU_TANH: out bf16 [M, N] = gelu_tanh(v); EPI_GATED_RESIDUAL: out fp32 [M, N]

@@ -415,3 +415,41 @@ def test_interleave_halves_round_trip():
     assert torch.equal(wi[256:384], w[128:256])
     x = torch.randn(7, 40, dtype=torch.float64)
     assert torch.allclose(deinterleave_halves(x @ wi.double().T, 128), x @ w.double().T)
+
+
+@gpu
+@needs_cuda
+def test_product_reads_the_attention_output():
+    """From 1536 rows the out projection reads the attention's output o [B, H, J, 128] itself through a 4-D
+    tensor map (sc_linear_heads): the same operand rows as sd_attention_merge gathers, so the same bits, for
+    fp32 and bf16 outputs and for the gated residual."""
+    import siliconed_b200.dit as dit
+    from siliconed_b200.products import Context
+    ctx = Context(0)
+    g = torch.Generator(device="cuda").manual_seed(31)
+    batch, heads, joint, off, n = 2, 2, 900, 100, 768
+    lin = dit.Linear(ctx, 640, heads * 128, g, bias=True)
+    o = torch.randn(batch, heads, joint, 128, generator=g, device="cuda").to(torch.bfloat16)
+    rows = batch * n
+    ws = torch.empty(lin.workspace_bytes(rows), dtype=torch.uint8, device="cuda")
+    merged = torch.empty(rows, heads * 128, dtype=torch.bfloat16, device="cuda")
+    scratch = torch.empty(rows, 640, device="cuda")
+    gate = torch.randn(640, generator=g, device="cuda")
+    r0 = torch.randn(rows, 640, generator=g, device="cuda")
+    outs = {}
+    try:
+        for fused in (True, False):
+            dit.FUSED_EPILOGUES = fused
+            y32 = lin.from_heads(o, off, n, torch.empty(rows, 640, device="cuda"), merged, ws).clone()
+            y16 = lin.from_heads(o, off, n, torch.empty(rows, 640, dtype=torch.bfloat16, device="cuda"), merged, ws)
+            r = r0.clone()
+            lin.gated_residual_heads(o, off, n, r, gate, merged, scratch, ws)
+            outs[fused] = (y32, y16.clone(), r)
+    finally:
+        dit.FUSED_EPILOGUES = True
+    torch.cuda.synchronize()
+    ctx.poll_errors()
+    for a, b in zip(outs[True], outs[False]):
+        assert torch.equal(a, b)
+    lin.close()
+    ctx.close()
