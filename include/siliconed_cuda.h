@@ -198,7 +198,8 @@ SC_API sc_status sc_quantize_rows(sc_ctx* ctx, const void* x, sc_in_type x_type,
 /* Operation fused into the epilogue of sc_linear_epilogue, applied to v = acc * s[n] + bias[n] (fp32). */
 typedef enum sc_epilogue {
     SC_EPI_GELU_TANH = 1,       /* y bf16 [m, n] = bf16(gelu_tanh(v)): one rounding instead of two */
-    SC_EPI_GATED_RESIDUAL = 2,  /* y fp32 [m, n] (read and written) = fmaf(gate[n], v, y) */
+    SC_EPI_GATED_RESIDUAL = 2,  /* y fp32 [m, n] (read and written) = y + gate[n] * v, two roundings
+                                   (Ops.gatedResidual, Ops.swift:44-54) */
     SC_EPI_SWIGLU = 3           /* W's columns in blocks of 128, gate block j then up block j (N a multiple of
                                    256): y bf16 [m, n / 2], y[:, 128 j + c] = bf16(silu(a) * b),
                                    a = v[:, 256 j + c], b = v[:, 256 j + 128 + c], silu(a) = a / (1 + exp(-a)) */

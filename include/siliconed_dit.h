@@ -45,6 +45,13 @@ SD_API int sd_layer_norm_modulate(const float* x, int64_t rows, int d, const flo
 SD_API int sd_gated_residual(float* x, const float* y, int64_t rows, int d, const float* gate, int gate_tanh,
                              const float* norm_weight, float eps, void* stream);
 
+/* sd_gated_residual, then sd_rms_norm_modulate(x, weight, scale, eps2, out) on the updated rows, in one pass
+ * (the Z-Image block's attention residual followed by the feed-forward's input norm): x is read once, updated
+ * in place and normalised from the same values; the bits of the two calls. */
+SD_API int sd_gated_residual_rms_modulate(float* x, const float* y, int64_t rows, int d, const float* gate,
+                                          int gate_tanh, const float* norm_weight, float eps, const float* weight,
+                                          const float* scale, float eps2, uint16_t* out, void* stream);
+
 /* One stream's fused QKV rows -> the attention's operands.  qkv bf16 [batch * tokens, 3 * heads * head_dim]
  * (q | k | v per token).  q and k: RMSNorm over head_dim with norm_q / norm_k (eps), then RoPE on adjacent
  * pairs with freqs fp32 [joint_len, head_dim / 2, 2] (cos, sin) at the token's joint position

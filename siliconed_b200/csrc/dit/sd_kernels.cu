@@ -141,11 +141,70 @@ __global__ void __launch_bounds__(kRowThreads) gated_residual_k(float* __restric
       o = make_float4(o.x * inv * w.x, o.y * inv * w.y, o.z * inv * w.z, o.w * inv * w.w);
     }
     float4 a = xr[i];
-    a.x = fmaf(g.x, o.x, a.x);
-    a.y = fmaf(g.y, o.y, a.y);
-    a.z = fmaf(g.z, o.z, a.z);
-    a.w = fmaf(g.w, o.w, a.w);
+    a.x = __fadd_rn(a.x, __fmul_rn(g.x, o.x));  // two roundings, as torch's x + gate * y
+    a.y = __fadd_rn(a.y, __fmul_rn(g.y, o.y));
+    a.z = __fadd_rn(a.z, __fmul_rn(g.z, o.z));
+    a.w = __fadd_rn(a.w, __fmul_rn(g.w, o.w));
     xr[i] = a;
+  }
+}
+
+// gated_residual_k followed by rms_norm_modulate_k on the updated row, in one pass: the row of x is read
+// once, updated, written, and normalised from the same registers (the same operations in the same order
+// as the two kernels, so the same bits).
+__global__ void __launch_bounds__(kRowThreads)
+    gated_residual_rms_modulate_k(float* __restrict__ x, const float* __restrict__ y, int d,
+                                  const float* __restrict__ gate, int gate_tanh,
+                                  const float* __restrict__ norm_weight, float eps,
+                                  const float* __restrict__ weight, const float* __restrict__ scale, float eps2,
+                                  uint16_t* __restrict__ out) {
+  __shared__ float red[kRowThreads / 32];
+  const int64_t r = blockIdx.x;
+  const int d4 = d / 4;
+  float4 v[kMaxVec];
+  load_row(y + r * d, d4, v);
+  float inv = 1.0f;
+  if (norm_weight != nullptr) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxVec; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+    inv = 1.0f / sqrtf(block_sum(ss, red) / static_cast<float>(d) + eps);
+  }
+  float4* xr = reinterpret_cast<float4*>(x + r * d);
+  float ss2 = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    const int i = threadIdx.x + j * kRowThreads;
+    if (i >= d4) {
+      v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      continue;
+    }
+    float4 g = vec_or(gate, i, 1.0f);
+    if (gate != nullptr && gate_tanh) g = make_float4(tanhf(g.x), tanhf(g.y), tanhf(g.z), tanhf(g.w));
+    float4 o = v[j];
+    if (norm_weight != nullptr) {
+      const float4 w = reinterpret_cast<const float4*>(norm_weight)[i];
+      o = make_float4(o.x * inv * w.x, o.y * inv * w.y, o.z * inv * w.z, o.w * inv * w.w);
+    }
+    float4 a = xr[i];
+    a.x = __fadd_rn(a.x, __fmul_rn(g.x, o.x));  // two roundings, as torch's x + gate * y
+    a.y = __fadd_rn(a.y, __fmul_rn(g.y, o.y));
+    a.z = __fadd_rn(a.z, __fmul_rn(g.z, o.z));
+    a.w = __fadd_rn(a.w, __fmul_rn(g.w, o.w));
+    xr[i] = a;
+    v[j] = a;
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) ss2 += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  const float inv2 = 1.0f / sqrtf(block_sum(ss2, red) / static_cast<float>(d) + eps2);
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    const int i = threadIdx.x + j * kRowThreads;
+    if (i >= d4) break;
+    const float4 w = vec_or(weight, i, 1.0f);
+    const float4 s = vec_or(scale, i, 0.0f);
+    store_bf16x4(out + r * d, i, v[j].x * inv2 * w.x * (1.0f + s.x), v[j].y * inv2 * w.y * (1.0f + s.y),
+                 v[j].z * inv2 * w.z * (1.0f + s.z), v[j].w * inv2 * w.w * (1.0f + s.w));
   }
 }
 
@@ -290,6 +349,19 @@ int sd_layer_norm_modulate(const float* x, int64_t rows, int d, const float* sca
   if (rows == 0) return SD_OK;
   layer_norm_modulate_k<<<static_cast<unsigned>(rows), kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       x, d, scale, shift, eps, out);
+  return status_of(cudaGetLastError());
+}
+
+int sd_gated_residual_rms_modulate(float* x, const float* y, int64_t rows, int d, const float* gate, int gate_tanh,
+                                   const float* norm_weight, float eps, const float* weight, const float* scale,
+                                   float eps2, uint16_t* out, void* stream) {
+  if (!row_args_ok(x, rows, d) || y == nullptr || !aligned(y, 16) || (gate && !aligned(gate, 16)) ||
+      (norm_weight && !aligned(norm_weight, 16)) || (weight && !aligned(weight, 16)) || (scale && !aligned(scale, 16)) ||
+      out == nullptr || !aligned(out, 16) || rows > 0x7FFFFFFF)
+    return SD_INVALID_ARG;
+  if (rows == 0) return SD_OK;
+  gated_residual_rms_modulate_k<<<static_cast<unsigned>(rows), kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, y, d, gate, gate_tanh, norm_weight, eps, weight, scale, eps2, out);
   return status_of(cudaGetLastError());
 }
 

@@ -63,7 +63,7 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 //
 // kOp: the epilogue's operation after v = acc * scale + bias (fp32).  kOpNone stores v; kOpGelu stores
 // bf16(gelu_tanh(v)) (one rounding, where a separate pass would round v first); kOpResidual adds
-// gate[n] * v to the fp32 output in place, x = fma(gate, v, x) (the gated residual stream).
+// gate[n] * v to the fp32 output in place, x = x + gate * v in two roundings (the gated residual stream).
 // kOpQkRope: the q / k / v product of a DiT block; each 128-column half of a tile is one head of q, k or
 // v.  For q and k the head is RMS-normalised over its 128 values (sum of squares from a first pass over
 // the accumulator, inv = 1 / sqrt(ss / 128 + eps), then * inv * norm[d]) and rotated by RoPE on adjacent
@@ -426,13 +426,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint4 u = st[rr * 8 + (cu ^ (rr & 7))];
               float* dst = static_cast<float*>(y_out) + static_cast<int64_t>(grow) * N + col;
               if (kOp == kOpResidual) {
-                // x = fmaf(gate, v, x): the fp32 residual stream, in place (the tile lies inside N)
+                // x = x + gate * v in two roundings (torch's x + gate * y, Ops.gatedResidual): the fp32
+                // residual stream, in place (the tile lies inside N)
                 if (grow < M) {
                   const float* g = s.sb2[ew] + ch * 32 + cu * 4;
                   const float4 xv = xcur[it];
-                  *reinterpret_cast<float4*>(dst) =
-                      make_float4(__fmaf_rn(g[0], __uint_as_float(u.x), xv.x), __fmaf_rn(g[1], __uint_as_float(u.y), xv.y),
-                                  __fmaf_rn(g[2], __uint_as_float(u.z), xv.z), __fmaf_rn(g[3], __uint_as_float(u.w), xv.w));
+                  *reinterpret_cast<float4*>(dst) = make_float4(
+                      __fadd_rn(xv.x, __fmul_rn(g[0], __uint_as_float(u.x))), __fadd_rn(xv.y, __fmul_rn(g[1], __uint_as_float(u.y))),
+                      __fadd_rn(xv.z, __fmul_rn(g[2], __uint_as_float(u.z))), __fadd_rn(xv.w, __fmul_rn(g[3], __uint_as_float(u.w))));
                 }
               } else if (grow < M) {
                 if (col + 4 <= N) {
@@ -453,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (kOp == kOpResidual) {
               const float* g = s.sb2[ew] + ch * 32;
               for (int j = 0; j < 32; ++j)
-                if (n + j < N) dst[j] = __fmaf_rn(g[j], __uint_as_float(r[j]), dst[j]);
+                if (n + j < N) dst[j] = __fadd_rn(dst[j], __fmul_rn(g[j], __uint_as_float(r[j])));
             } else {
               for (int j = 0; j < 32; ++j)
                 if (n + j < N) dst[j] = __uint_as_float(r[j]);

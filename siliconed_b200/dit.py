@@ -260,9 +260,9 @@ class ZImageBlock:
                            ws)
         o = attention(b["q"], b["k"], b["v"])
         self.out.from_heads(o, 0, s, b["y"], b["merged"], ws)
-        dk.gated_residual(x, b["y"], gate_msa, True, self.norm2, self.eps)
-        # feed-forward
-        dk.rms_norm_modulate(x, self.ffn_norm1, scale_mlp, self.eps, b["a"])
+        # the attention's residual and the feed-forward's input norm in one pass
+        dk.gated_residual_rms_modulate(x, b["y"], gate_msa, True, self.norm2, self.eps, self.ffn_norm1, scale_mlp,
+                                       self.eps, b["a"])
         self.w13.swiglu(b["a"], b["g"], b["h"], ws)
         self.w2(b["g"], b["y"], ws)
         dk.gated_residual(x, b["y"], gate_mlp, True, self.ffn_norm2, self.eps)

@@ -19,6 +19,7 @@ SIGNATURES = {
     "sd_rms_norm_modulate": (_I, [_P, _I64, _I, _P, _P, _F, _P, _P]),
     "sd_layer_norm_modulate": (_I, [_P, _I64, _I, _P, _P, _F, _P, _P]),
     "sd_gated_residual": (_I, [_P, _P, _I64, _I, _P, _I, _P, _F, _P]),
+    "sd_gated_residual_rms_modulate": (_I, [_P, _P, _I64, _I, _P, _I, _P, _F, _P, _P, _F, _P, _P]),
     "sd_qk_norm_rope": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _F, _P, _P, _P, _I, _I, _P]),
     "sd_attention_merge": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "sd_swiglu": (_I, [_P, _I64, _I, _P, _P]),
@@ -88,6 +89,14 @@ def gated_residual(x, y, gate, gate_tanh: bool, norm_weight, eps):
     _check(load().sd_gated_residual(_ptr(x), _ptr(y), rows, d, _ptr(gate), int(gate_tanh), _ptr(norm_weight), eps,
                                     _stream()), "sd_gated_residual")
     return x
+
+
+def gated_residual_rms_modulate(x, y, gate, gate_tanh: bool, norm_weight, eps, weight, scale, eps2, out):
+    rows, d = x.shape
+    _check(load().sd_gated_residual_rms_modulate(_ptr(x), _ptr(y), rows, d, _ptr(gate), int(gate_tanh),
+                                                 _ptr(norm_weight), eps, _ptr(weight), _ptr(scale), eps2, _ptr(out),
+                                                 _stream()), "sd_gated_residual_rms_modulate")
+    return out
 
 
 def qk_norm_rope(qkv, batch, tokens, heads, norm_q, norm_k, freqs, eps, q, k, v, joint_len, token_offset):

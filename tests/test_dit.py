@@ -244,7 +244,7 @@ def test_mmdit_block_matches_fp32_reference():
 @needs_cuda
 def test_fused_epilogues_agree_with_the_separate_stages():
     """From 1536 rows the MMDiT block's gated residuals and GELU run in the product's epilogue: the
-    gated residual bit for bit as the product plus sd_gated_residual (both fmaf(gate, v, x)); the GELU
+    gated residual bit for bit as the product plus sd_gated_residual (both x + gate * v in two roundings); the GELU
     within one bf16 rounding of the product's bf16 output run through sd_gelu_tanh (the separate
     stages round v to bf16 first, which moves gelu by up to 1.2 |v| 2^-8)."""
     import siliconed_b200.dit as dit
@@ -453,3 +453,22 @@ def test_product_reads_the_attention_output():
         assert torch.equal(a, b)
     lin.close()
     ctx.close()
+
+
+@gpu
+@needs_cuda
+def test_gated_residual_then_rms_modulate_in_one_pass():
+    """sd_gated_residual_rms_modulate gives the bits of sd_gated_residual followed by sd_rms_norm_modulate."""
+    g = torch.Generator(device="cuda").manual_seed(41)
+    rows, d = 37, 3840
+    x0 = torch.randn(rows, d, generator=g, device="cuda")
+    y = torch.randn(rows, d, generator=g, device="cuda")
+    gate, nw = torch.randn(d, generator=g, device="cuda"), torch.rand(d, generator=g, device="cuda") + 0.5
+    w2, sc = torch.rand(d, generator=g, device="cuda") + 0.5, torch.randn(d, generator=g, device="cuda") * 0.1
+    xa, a1 = x0.clone(), torch.empty(rows, d, dtype=torch.bfloat16, device="cuda")
+    dit_abi.gated_residual(xa, y, gate, True, nw, 1e-5)
+    dit_abi.rms_norm_modulate(xa, w2, sc, 1e-6, a1)
+    xb, a2 = x0.clone(), torch.empty(rows, d, dtype=torch.bfloat16, device="cuda")
+    dit_abi.gated_residual_rms_modulate(xb, y, gate, True, nw, 1e-5, w2, sc, 1e-6, a2)
+    torch.cuda.synchronize()
+    assert torch.equal(xa, xb) and torch.equal(a1.view(torch.int16), a2.view(torch.int16))

@@ -111,7 +111,7 @@ def test_rotated_products_match_oracle(ctx, m, k, n):
     witness = oracle.bf16_to_f32(x).astype(np.float64) @ wr + oracle.bf16_to_f32(b)
     assert rel_l2(got32, witness) <= 5e-3
     if m > 128:
-        # the fused gated residual on the same rotated operand: fmaf(gate, v, x)
+        # the fused gated residual on the same rotated operand: x + gate * v
         gate = torch.randn(n, device="cuda")
         r0 = torch.randn(m, n, device="cuda")
         r = r0.clone()
