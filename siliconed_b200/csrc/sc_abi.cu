@@ -240,6 +240,16 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
         (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0) {
       CUtensorMap tmw;
       if ((s = make_tmap_widened(ctx, w, workspace, &tmw)) != SC_OK) return s;
+      if (fused_widen_fits(w, m, ctx->sm_count)) {
+        // a few rounds of tiles: the GEMM's CTAs widen the codes themselves, the first round's columns
+        // first, the rest while the pipeline runs
+        uint32_t* bank = ctx->d_widen + ctx->widen_bank * kWidenBankWords;
+        uint32_t* next = ctx->d_widen + (1 - ctx->widen_bank) * kWidenBankWords;
+        ctx->widen_bank ^= 1;
+        return check_cuda(ctx, launch_gemm_bf16_fw(tmx, tmw, w, bias, y, f32_out, workspace, bank, next, m,
+                                                   ctx->d_err, ctx->sm_count, st),
+                          "bf16 pair gemm (fused widening) launch");
+      }
       if ((s = check_cuda(ctx, launch_widen(w, workspace, ctx->sm_count, st), "widen launch")) != SC_OK) return s;
       return check_cuda(ctx, launch_gemm_bf16(tmx, tmw, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
                         "bf16 pair gemm launch");
@@ -307,9 +317,12 @@ sc_status sc_ctx_create(int device, sc_ctx** out) {
   }
   ctx->encode_tiled = reinterpret_cast<sc_encode_tiled_fn>(fn);
   if (cudaMalloc(&ctx->d_err, kCtxWords * sizeof(int)) != cudaSuccess ||
-      cudaMemset(ctx->d_err, 0, kCtxWords * sizeof(int)) != cudaSuccess) {
+      cudaMemset(ctx->d_err, 0, kCtxWords * sizeof(int)) != cudaSuccess ||
+      cudaMalloc(&ctx->d_widen, 2 * kWidenBankWords * sizeof(uint32_t)) != cudaSuccess ||
+      cudaMemset(ctx->d_widen, 0, 2 * kWidenBankWords * sizeof(uint32_t)) != cudaSuccess) {
     cudaGetLastError();
     if (ctx->d_err) cudaFree(ctx->d_err);
+    if (ctx->d_widen) cudaFree(ctx->d_widen);
     delete ctx;
     return SC_OUT_OF_MEMORY;
   }
@@ -323,6 +336,7 @@ void sc_ctx_destroy(sc_ctx* ctx) {
   cudaGetDevice(&cur);
   cudaSetDevice(ctx->device);
   if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->d_widen) cudaFree(ctx->d_widen);
   for (cudaEvent_t e : ctx->host_events)
     if (e) cudaEventDestroy(e);
   if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);

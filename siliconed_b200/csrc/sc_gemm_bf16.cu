@@ -97,13 +97,20 @@ __device__ __forceinline__ float epi_value(uint32_t raw, float sc, float bi, flo
 
 // kI8: both operands int8 codes (x's per-row codes, the weight's codes made signed), 128 codes = 128
 // bytes per K stage, tcgen05.mma kind::i8 into s32 accumulators; row_scales holds s_x per row.
-template <bool kF32Out, bool kPeers, int kOp, bool kI8>
+// kFW (fused widening, 1 int8 / 2 e4m3 / 3 e4m3 with NaN codes): the CTAs widen the codes themselves.
+// Every thread first widens the column blocks the first round of tiles reads; then warps 2-7 widen the
+// rest, block by block, while the pipeline runs (warps 2 and 3 are otherwise idle, and the epilogue warps
+// have nothing to do until the first accumulator is ready).  After its share of a block, a CTA counts
+// itself on the block's counter; a producer waits for all CTAs on the block of its tile before the
+// tile's first load (acquire, then a proxy fence: the data was written by ordinary stores).
+template <bool kF32Out, bool kPeers, int kOp, bool kI8, int kFW = 0>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_pair(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const float* __restrict__ scales, const uint16_t* __restrict__ bias, void* __restrict__ y_out,
                    int M, int N, int k_tiles, int m_tiles, int n_tiles, int* err,
                    const __grid_constant__ PeerOut peers, const float* __restrict__ gate,
-                   const float* __restrict__ row_scales, const __grid_constant__ HeadOut ho, const XHeads xh) {
+                   const float* __restrict__ row_scales, const __grid_constant__ HeadOut ho, const XHeads xh,
+                   const __grid_constant__ FusedWiden fw) {
   static_assert(kOp != kOpResidual || kF32Out, "the residual is fp32");
   static_assert(kOp != kOpGelu || !kF32Out, "the GELU output is bf16");
   static_assert(!kI8 || (kOp == kOpNone && !kPeers), "W8A8 stores plain outputs");
@@ -144,17 +151,60 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Launched early behind the widening (or the int8 passes) of the same product, the set-up above
   // overlapped their end; nothing reads or writes global memory before this point.
   pdl_wait();
+  if (kFW != 0) {
+    if (blockIdx.x == 0)
+      for (int i = threadIdx.x; i < fw.n_blocks; i += kThreads) fw.next_bank[i] = 0;
+    // every thread of the grid: the first round's column blocks
+    const int64_t n0 = static_cast<int64_t>(fw.first_blocks) * fw.chunks_per_block;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; base < n0; base += 4 * stride) {
+      uint4 in[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = base + u * stride;
+        in[u] = i < n0 ? __ldcs(fw.codes + i) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = base + u * stride;
+        if (i < n0) {
+          uint4 lo, hi;
+          codes16_to_bf16<kFW == 1 ? 1 : 2, kFW == 3>(in[u], lo, hi);
+          fw.out[2 * i] = lo;
+          fw.out[2 * i + 1] = hi;
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      for (int b = 0; b < fw.first_blocks; ++b) atomicAdd(fw.counters + b, 1u);
+    }
+  }
 
   if (warp == 0) {
     // ---------------- TMA producer (each CTA loads its own halves) ----------------
     if (lane == 0) {
-      int stage = 0;
+      int stage = 0, ready_block = -1;
       uint32_t phase = 0, issued = 0, last_parity = 0;
       for (int tile = pair; tile < num_tiles && !*abort; tile += pairs) {
         int mt, nt;
         tile_coords(tile, m_tiles, n_tiles, mt, nt);
         const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM;
         const int col0 = nt * BN + static_cast<int>(rank) * BNH;
+        if (kFW != 0 && nt != ready_block) {
+          // the tile's column block widened by every CTA (bounded wait)
+          const unsigned long long t0 = global_ns();
+          while (ld_acquire_gpu(fw.counters + nt) < gridDim.x) {
+            if (global_ns() - t0 > kWaitLimitNs) {
+              record_error(err, kErrTimeout, kSiteWidened);
+              *abort = 1;
+              break;
+            }
+          }
+          fence_proxy_async_global();
+          ready_block = nt;
+        }
         for (int kt = 0; kt < k_tiles; ++kt) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort, err, kSiteProducerEmpty)) break;
           if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (kABytes + kBBytes));
@@ -222,7 +272,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit_pair(peer_addr(&s.drain, 0));
       mbar_wait_drain(&s.drain, 0);
     }
-  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
+  }
+  if (kFW != 0 && warp >= 2) {
+    // the remaining column blocks, each CTA its slice of every block, in block order
+    const int t = threadIdx.x - 64, nt_threads = kThreads - 64;
+    // (no early exit: every warp of 2..7 must reach each block's named barrier)
+    for (int b = fw.first_blocks; b < fw.n_blocks; ++b) {
+      const int64_t c0 = static_cast<int64_t>(b) * fw.chunks_per_block +
+                         static_cast<int64_t>(blockIdx.x) * fw.chunks_per_block / gridDim.x;
+      const int64_t c1 = static_cast<int64_t>(b) * fw.chunks_per_block +
+                         static_cast<int64_t>(blockIdx.x + 1) * fw.chunks_per_block / gridDim.x;
+      for (int64_t base = c0 + t; base < c1; base += 2 * nt_threads) {
+        const int64_t i1 = base + nt_threads;
+        const uint4 in0 = __ldcs(fw.codes + base);
+        const uint4 in1 = i1 < c1 ? __ldcs(fw.codes + i1) : make_uint4(0, 0, 0, 0);
+        uint4 lo, hi;
+        codes16_to_bf16<kFW == 1 ? 1 : 2, kFW == 3>(in0, lo, hi);
+        fw.out[2 * base] = lo;
+        fw.out[2 * base + 1] = hi;
+        if (i1 < c1) {
+          codes16_to_bf16<kFW == 1 ? 1 : 2, kFW == 3>(in1, lo, hi);
+          fw.out[2 * i1] = lo;
+          fw.out[2 * i1 + 1] = hi;
+        }
+      }
+      named_barrier_sync(2, kThreads - 64);
+      if (t == 0) {
+        __threadfence();
+        atomicAdd(fw.counters + b, 1u);
+      }
+    }
+  }
+  if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
     // ---------------- epilogue (each CTA: its 128 rows x 256 columns) ----------------
     const int ew = warp - kEpiWarp0;
     float* s_scale = s.sb[ew][0];
@@ -582,14 +663,15 @@ __global__ void __launch_bounds__(256) widen_codes(const uint4* __restrict__ cod
   }
 }
 
-template <bool kF32Out, bool kPeers, int kOp = kOpNone, bool kI8 = false>
+template <bool kF32Out, bool kPeers, int kOp = kOpNone, bool kI8 = false, int kFW = 0>
 cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const sc_weight* w, const uint16_t* bias,
                         void* y, int64_t m, int* err, int sm_count, cudaStream_t stream, const PeerOut& peers,
                         const float* gate = nullptr, const float* row_scales = nullptr, const HeadOut* heads = nullptr,
-                        const XHeads* x_heads = nullptr) {
+                        const XHeads* x_heads = nullptr, const FusedWiden* fwp = nullptr) {
   const HeadOut ho = heads != nullptr ? *heads : HeadOut{};
+  FusedWiden fw = fwp != nullptr ? *fwp : FusedWiden{};
   const XHeads xh = x_heads != nullptr ? *x_heads : XHeads{0, 0};
-  auto kernel = gemm_bf16_pair<kF32Out, kPeers, kOp, kI8>;
+  auto kernel = gemm_bf16_pair<kF32Out, kPeers, kOp, kI8, kFW>;
   static unsigned long long configured = 0;  // per template instance and device
   if (cudaError_t e = set_smem_once(kernel, static_cast<int>(kSmemBytes), configured); e != cudaSuccess) return e;
   const int m_tiles = static_cast<int>((m + 2 * BM - 1) / (2 * BM));
@@ -598,8 +680,38 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   // reads zeros (the copy's fill), as x's codes are zero past K.
   const int k_tiles = static_cast<int>(kI8 ? (w->k_pad + 127) / 128 : w->k_pad / BK);
   const int tiles = m_tiles * n_tiles;
-  const int max_pairs = sm_count / 2;
+  int max_pairs = sm_count / 2;
+  if (kFW != 0) {
+    // The fused widening's waits need every CTA resident at once: no more pairs than the device holds
+    // as co-resident clusters of this kernel (asked once per device).
+    static int resident[64] = {0};
+    int dev = 0;
+    if (cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return e;
+    if (resident[dev & 63] == 0) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(static_cast<unsigned>(2 * max_pairs), 1, 1);
+      q.blockDim = dim3(kThreads, 1, 1);
+      q.dynamicSmemBytes = kSmemBytes;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = 2;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      q.attrs = qa;
+      q.numAttrs = 1;
+      int n = 0;
+      if (cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kernel, &q); e != cudaSuccess) return e;
+      resident[dev & 63] = n > 0 ? n : 1;
+    }
+    if (resident[dev & 63] < max_pairs) max_pairs = resident[dev & 63];
+  }
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  if (kFW != 0) {
+    // One group of the tile order (m_tiles <= 16): tile t has column block t / m_tiles, so the first round
+    // (tiles 0 .. pairs - 1) reads blocks 0 .. (pairs - 1) / m_tiles.
+    fw.first_blocks = (pairs - 1) / m_tiles + 1;
+    if (fw.first_blocks > fw.n_blocks) fw.first_blocks = fw.n_blocks;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -618,7 +730,7 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias, y,
                             static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers, gate,
-                            row_scales, ho, xh);
+                            row_scales, ho, xh, fw);
 }
 
 // The weight's arena codes (int8 stored biased by 128) made signed again for the int8 MMA: code ^ 0x80.
@@ -682,6 +794,42 @@ cudaError_t launch_gemm_bf16(const CUtensorMap& tmap_x, const CUtensorMap& tmap_
   const PeerOut none = {};
   return f32_out ? gemm_bf16::launch_gemm<true, false>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream, none)
                  : gemm_bf16::launch_gemm<false, false>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, stream, none);
+}
+
+bool fused_widen_fits(const sc_weight* w, int64_t m, int sm_count) {
+  using namespace gemm_bf16;
+  const int64_t m_tiles = (m + 2 * BM - 1) / (2 * BM), n_tiles = w->n_pad / BN;
+  // Two to three rounds of pair tiles: there the separate widening was a sixth of the product (config 1:
+  // 10 of 74 us; 70 us with it inside).  With more rounds its share shrinks and the blocks widened during
+  // the run fall behind the tiles that need them (config 2, 8.6 rounds: 259 us inside against 233 apart).
+  const int64_t tiles = m_tiles * n_tiles, pairs = sm_count / 2;
+  return m_tiles <= kTileGroupRows && tiles >= 2 * pairs && tiles <= 3 * pairs && n_tiles <= kWidenBankWords;
+}
+
+cudaError_t launch_gemm_bf16_fw(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
+                                const uint16_t* bias, void* y, bool f32_out, void* widened, uint32_t* counters,
+                                uint32_t* next_bank, int64_t m, int* err, int sm_count, cudaStream_t stream) {
+  using namespace gemm_bf16;
+  const PeerOut none = {};
+  FusedWiden fw;
+  fw.codes = reinterpret_cast<const uint4*>(w->values);
+  fw.out = static_cast<uint4*>(widened);
+  fw.counters = counters;
+  fw.next_bank = next_bank;
+  fw.chunks_per_block = static_cast<int>(BN * w->k_pad / 16);
+  fw.n_blocks = static_cast<int>(w->n_pad / BN);
+  fw.first_blocks = 0;  // set by launch_gemm from the pairs it launches
+#define SC_FW_LAUNCH(KIND)                                                                                   \
+  return f32_out ? launch_gemm<true, false, kOpNone, false, KIND>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, \
+                                                                   stream, none, nullptr, nullptr, nullptr,  \
+                                                                   nullptr, &fw)                              \
+                 : launch_gemm<false, false, kOpNone, false, KIND>(tmap_x, tmap_w, w, bias, y, m, err, sm_count, \
+                                                                    stream, none, nullptr, nullptr, nullptr, \
+                                                                    nullptr, &fw)
+  if (w->kind == SC_WEIGHT_INT8) SC_FW_LAUNCH(1);
+  if (w->has_nan_codes) SC_FW_LAUNCH(3);
+  SC_FW_LAUNCH(2);
+#undef SC_FW_LAUNCH
 }
 
 cudaError_t launch_gemm_bf16_xheads(const CUtensorMap& tmap_o, const CUtensorMap& tmap_w, const sc_weight* w,

@@ -47,6 +47,10 @@ struct sc_ctx {
                          // fused gather's CTA counter (zero between launches)
   sc_encode_tiled_fn encode_tiled = nullptr;
   std::string last_error;
+  // The fused widening's readiness counters: two banks of kWidenBankWords, zeroed at creation; calls
+  // alternate banks (each call zeroes the other one for the next).
+  uint32_t* d_widen = nullptr;
+  int widen_bank = 0;
   // sc_linear_host's copy streams and events, created on its first call and kept with the context.
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
   cudaEvent_t host_events[2 * 32 + 2] = {};
@@ -131,6 +135,26 @@ struct HeadOut {
 // x given as the attention's output o [batch, heads, joint, 128] (a 4-D tensor map): the product's row r is
 // token r % tokens of image r / tokens at position offset + r % tokens, K = heads * 128.  tokens 0: x is a
 // plain [M, K] matrix.
+// The widening done inside the bf16 pair GEMM (launch_gemm_bf16_fw): codes -> the workspace's bf16 copy
+// by the GEMM's own CTAs, column block by column block, each block's readiness counted in counters[block]
+// (this call's bank, zero at launch; the kernel zeroes next_bank for the next call).
+struct FusedWiden {
+  const uint4* codes;
+  uint4* out;
+  uint32_t* counters;
+  uint32_t* next_bank;
+  int chunks_per_block;  // 256 * k_pad / 16: 16-code chunks of one 256-column block
+  int first_blocks;      // the blocks the first round of tiles reads, widened by every thread first
+  int n_blocks;          // n_pad / 256
+};
+constexpr int kWidenBankWords = 1024;  // column blocks per counter bank (N up to 262144)
+cudaError_t launch_gemm_bf16_fw(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
+                                const uint16_t* bias, void* y, bool f32_out, void* widened, uint32_t* counters,
+                                uint32_t* next_bank, int64_t m, int* err, int sm_count, cudaStream_t stream);
+// Whether launch_gemm_bf16_fw serves a product of m rows: two to three rounds of pair tiles, one group of
+// the tile order (m_tiles <= 16).
+bool fused_widen_fits(const sc_weight* w, int64_t m, int sm_count);
+
 struct XHeads {
   int tokens, offset;
 };

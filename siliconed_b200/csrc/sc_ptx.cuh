@@ -26,6 +26,7 @@ enum WaitSite : int {
   kSiteEpilogueFull = 7,
   kSiteDrain = 8,
   kSiteGather = 9,
+  kSiteWidened = 10,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -144,6 +145,16 @@ __device__ __forceinline__ float4 ld_cg_f4(const float* p) {
   asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
   return v;
 }
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Orders this thread's earlier global accesses (the acquire of a flag) before its later async-proxy
+// accesses (TMA reads of data other CTAs wrote with ordinary stores).
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;

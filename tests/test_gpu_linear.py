@@ -390,7 +390,10 @@ def test_fused_pair_kernel_matches_oracle(ctx, kind, m, k, n):
 @pytest.mark.parametrize("kind,m,k,n,nan", [(abi.WEIGHT_INT8, 1536, 3072, 3072, False),
                                             (abi.WEIGHT_INT8, 4096, 512, 3072, False),
                                             (abi.WEIGHT_E4M3, 2000, 2048, 2560, False),
-                                            (abi.WEIGHT_E4M3, 1600, 512, 700, True)])
+                                            (abi.WEIGHT_E4M3, 1600, 512, 700, True),
+                                            # 160 pair tiles in one group: the widening inside the GEMM
+                                            (abi.WEIGHT_E4M3, 4096, 512, 2560, True),
+                                            (abi.WEIGHT_E4M3, 4096, 512, 2560, False)])
 def test_widened_and_fused_routes_agree(ctx, kind, m, k, n, nan):
     """The widened route (from 1536 rows, workspace given) and the fused kernel (none) give the
     same bits."""
