@@ -138,6 +138,13 @@ def route_kernels(case, ws_bytes: int) -> list[str]:
     if case.m <= 128:
         return ["gemm_w8_tc"]
     if ws_bytes > 0:
+        # 2 to 3 rounds of 256 x 256 pair tiles in one group of the tile order: the widening runs inside
+        # the GEMM (fused_widen_fits in the library)
+        import torch
+        pairs = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count // 2
+        m_tiles, n_tiles = -(-case.m // 256), -(-case.n // 256)
+        if m_tiles <= 16 and 2 * pairs <= m_tiles * n_tiles <= 3 * pairs:
+            return ["gemm_bf16_pair (widening inside)"]
         return ["widen_codes", "gemm_bf16_pair"]
     return ["gemm_w8_pair"]
 
