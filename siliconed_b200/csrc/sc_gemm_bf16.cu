@@ -17,7 +17,13 @@
 // barrier, and the leader issues tcgen05.mma.cta_group::2 (M = 256, N = 256) into the fp32
 // accumulators of both CTAs' TMEM (two buffers of 256 columns: the epilogue of one tile overlaps
 // the MMAs of the next).  Warp 0: TMA producer; warp 1: TMEM allocation and (leader) MMA issue;
-// warps 4..7: epilogue.  No load uses cluster multicast; every wait is bounded.
+// warps 4..7: epilogue; warps 2..7 also widen codes in the kFW variant.  No load uses cluster
+// multicast; every wait is bounded.
+//
+// Variants (template parameters): fp32 or bf16 output; the epilogue's operation (kOp: none, GELU, gated
+// residual, QK-norm + RoPE into the attention's layout, SwiGLU); the column-parallel gather's peer or
+// multicast stores (kPeers); int8 x int8 operands for W8A8 (kI8); the widening inside the kernel (kFW).
+// At run time the operand x can also be the attention's output read through a 4-D tensor map (XHeads).
 #include <cuda_bf16.h>
 
 #include "sc_codes.cuh"
