@@ -80,8 +80,9 @@ class Context:
         self.check(self.lib.sc_poll_errors(self.ptr, _stream_ptr(stream)))
 
 
-def _scale_type_of(scales) -> tuple[int, object]:
-    """(sc_scale_type, contiguous host-or-device buffer) of a scale array as published."""
+def _scale_type_of(scales, declared: int | None = None) -> tuple[int, object]:
+    """(sc_scale_type, contiguous host-or-device buffer) of a scale array as published; bf16 scales come
+    as a torch bfloat16 tensor, or as 16-bit integer bits with ``declared`` = SCALE_BF16."""
     if torch is not None and isinstance(scales, torch.Tensor):
         t = scales.contiguous()
         kinds = {torch.float32: abi.SCALE_F32, torch.bfloat16: abi.SCALE_BF16, torch.float16: abi.SCALE_F16}
@@ -89,6 +90,8 @@ def _scale_type_of(scales) -> tuple[int, object]:
             raise SiliconedError(abi.INVALID_ARG, f"scale dtype {t.dtype}")
         return kinds[t.dtype], t
     a = np.ascontiguousarray(scales)
+    if declared == abi.SCALE_BF16 and a.dtype in (np.dtype(np.uint16), np.dtype(np.int16)):
+        return abi.SCALE_BF16, a
     kinds = {np.dtype(np.float32): abi.SCALE_F32, np.dtype(np.float16): abi.SCALE_F16}
     if a.dtype not in kinds:
         raise SiliconedError(abi.INVALID_ARG, f"scale dtype {a.dtype} (pass bf16 bits with scale_type=SCALE_BF16)")
@@ -123,7 +126,7 @@ class QuantizedWeight:
         if len(shape) != 2:
             raise SiliconedError(abi.INVALID_ARG, "values must be 2-D")
         k, n = (shape[1], shape[0]) if published_nk else shape
-        st, s = _scale_type_of(scales)
+        st, s = _scale_type_of(scales, scale_type)
         if scale_type is not None:
             st = scale_type
         s_count = int(np.prod(s.shape)) if len(s.shape) else 1
@@ -379,6 +382,23 @@ class WeightProducts:
         if bias is not None:
             self.biases[name] = bias
         return w
+
+    def register_map(self, artifact, names=None, device=None) -> list[str]:
+        """Registers the 8-bit linears of an opened map (``artifact.Artifact``), all of them or ``names``,
+        each read in place from the mapped file (WeightProducts.inPlaceInt8, WeightProducts.swift:801-862).
+        A weight ``<base>.weight`` takes the map's ``<base>.bias`` when it is a bf16 vector of N values,
+        as a device tensor; any other bias stays the caller's to give.  Returns the names registered."""
+        names = artifact.quantized_names() if names is None else list(names)
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        for name in names:
+            w = artifact.register(self.ctx, name)
+            self.weights[name] = w
+            if name.endswith(".weight"):
+                b = artifact.tensors.get(name[: -len(".weight")] + ".bias")
+                if b is not None and b.dtype == "bfloat16" and b.shape == (w.n,):
+                    bits = np.array(artifact.array(b.name))  # a copy: the map stays read-only
+                    self.biases[name] = torch.from_numpy(bits.view(np.int16)).to(device).view(torch.bfloat16)
+        return names
 
     def linear(self, name: str, a, c, m: int, k: int, n: int, stream=None) -> None:
         w = self.weights.get(name)

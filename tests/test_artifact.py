@@ -1,0 +1,229 @@
+"""The map file (``SILICON``) reader and writer, on the CPU.
+
+Restates the reference's map tests: RobustnessTests.swift:20-126 (hand-written maps with 16-byte pages:
+a valid one reads; an aberrant header length, a page of zero or less, negative offsets and sizes, and
+overflowing shapes are refused as a damaged map; headerLength and elementCount at their bounds; refused
+opens leak no descriptor) and QuantizedMapTests.swift:149-216 (a published 8-bit linear forged to the
+map: the codes transposed byte for byte, the scales kept in their type at offset 48 after 36 values),
+plus the scale and rotation checks of Artifact.swift:378-418.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from siliconed_b200 import artifact
+from siliconed_b200.artifact import Artifact, MapError, MapTensor, element_count, header_length
+
+INT_MAX = (1 << 63) - 1
+
+
+def hand_map(tmp_path, header: dict, data=(1.0, 2.0, 3.0, 4.0), length: int | None = None, data_offset: int = 256,
+             raw_data: bytes | None = None) -> str:
+    """``SILICON`` v3, the header's length (or ``length``), the JSON, the data at ``data_offset``."""
+    text = json.dumps(header).encode()
+    body = b"SILICON" + bytes([3]) + (len(text) if length is None else length).to_bytes(8, "little") + text
+    assert len(body) <= data_offset, "header longer than the test's layout"
+    body += bytes(data_offset - len(body))
+    body += raw_data if raw_data is not None else np.asarray(data, np.float32).tobytes()
+    path = tmp_path / f"m-{abs(hash((text, length, data_offset, body[-8:])))}.silicon"
+    path.write_bytes(body)
+    return str(path)
+
+
+def header(page=16, offset=256, nbytes=16, shape=(4,)) -> dict:
+    return {"page": page, "order": ["w"],
+            "tensors": {"w": {"offset": offset, "bytes": nbytes, "shape": list(shape), "dtype": "float32"}}}
+
+
+def assert_corrupt(path: str) -> MapError:
+    with pytest.raises(MapError) as e:
+        Artifact(path)
+    assert e.value.path == path and e.value.kind != "cannot_open"
+    return e.value
+
+
+def test_a_valid_hand_written_map_reads(tmp_path):
+    with Artifact(hand_map(tmp_path, header())) as m:
+        assert m.order == ["w"] and m.page == 16
+        assert m.array("w").tolist() == [1, 2, 3, 4]
+
+
+def test_an_aberrant_header_length_is_refused(tmp_path):
+    for length in (2 ** 64 - 1, INT_MAX, 1 << 40, 100_000):
+        path = hand_map(tmp_path, header(), length=length)
+        assert_corrupt(path)
+        with pytest.raises(MapError):
+            Artifact.read_header(path)
+    assert header_length(2 ** 64 - 1, 1000) is None
+    assert header_length(985, 1000) is None
+    assert header_length(984, 1000) == 984
+
+
+def test_a_page_of_zero_or_less_is_refused(tmp_path):
+    assert_corrupt(hand_map(tmp_path, header(page=0)))
+    assert_corrupt(hand_map(tmp_path, header(page=-16)))
+
+
+def test_negative_offsets_and_sizes_are_refused(tmp_path):
+    assert_corrupt(hand_map(tmp_path, header(offset=-16)))
+    assert_corrupt(hand_map(tmp_path, header(offset=-4096)))
+    assert_corrupt(hand_map(tmp_path, header(nbytes=-16)))
+    assert_corrupt(hand_map(tmp_path, header(offset=INT_MAX // 16 * 16)))  # beyond the file, no overflow
+
+
+def test_a_shape_whose_count_overflows_is_refused(tmp_path):
+    assert_corrupt(hand_map(tmp_path, header(shape=(INT_MAX, 4))))
+    assert_corrupt(hand_map(tmp_path, header(shape=(-1, -4))))
+    assert element_count([INT_MAX, 2]) is None
+    assert element_count([3, -1]) is None
+    assert element_count([]) == 1
+    assert element_count([3, 0]) == 0
+
+
+def test_other_damage_is_named(tmp_path):
+    e = assert_corrupt(hand_map(tmp_path, header(offset=264)))
+    assert e.kind == "unaligned"
+    assert assert_corrupt(hand_map(tmp_path, header(nbytes=12))).kind == "bad_header"  # bytes disagree with shape
+    h = header()
+    h["order"] = ["w", "x"]
+    assert assert_corrupt(hand_map(tmp_path, h)).kind == "bad_header"
+    h = header()
+    h["tensors"]["w"]["dtype"] = "float64"
+    assert assert_corrupt(hand_map(tmp_path, h)).kind == "bad_header"
+    p = tmp_path / "short.silicon"
+    p.write_bytes(b"SILICON\x03")
+    assert assert_corrupt(str(p)).kind == "truncated"
+    p = tmp_path / "magic.silicon"
+    p.write_bytes(b"SILICON\x01" + bytes(40))
+    assert assert_corrupt(str(p)).kind == "bad_magic"
+    with pytest.raises(MapError) as e:
+        Artifact(str(tmp_path / "absent.silicon"))
+    assert e.value.kind == "cannot_open"
+
+
+def test_a_refused_map_leaks_no_descriptor(tmp_path):
+    bad = hand_map(tmp_path, header(page=0))
+    before = len(os.listdir("/proc/self/fd"))
+    for _ in range(3000):
+        with pytest.raises(MapError) as e:
+            Artifact(bad)
+        assert e.value.kind == "bad_header" and e.value.path == bad
+    assert len(os.listdir("/proc/self/fd")) == before
+    Artifact(hand_map(tmp_path, header())).close()
+
+
+def quantized_entry(offset=256, nbytes=60, shape=(6, 6), dtype="int8", scale=None, rotation=None) -> dict:
+    e = {"offset": offset, "bytes": nbytes, "shape": list(shape), "dtype": dtype,
+         "scale": scale if scale is not None else {"offset": 48, "dtype": "float16", "shape": [shape[1]]}}
+    if rotation is not None:
+        e["rotation"] = rotation
+    return e
+
+
+def test_scale_entries_are_checked_against_their_tensor(tmp_path):
+    def open_with(entry):
+        return Artifact(hand_map(tmp_path, {"page": 16, "tensors": {"w": entry}}, raw_data=bytes(entry["bytes"])))
+
+    m = open_with(quantized_entry())  # 36 values, 12 bytes of padding, 6 fp16 scales at 48: 60 bytes
+    t = m.tensor("w")
+    assert (t.scale.offset, t.scale.dtype, t.scale.shape, t.scale.layout) == (48, "float16", (6,), "columns")
+    m.close()
+    bad_scales = [
+        {"offset": 40, "dtype": "float16", "shape": [6]},            # not a multiple of 16
+        {"offset": 32, "dtype": "float16", "shape": [6]},            # inside the values
+        {"offset": 48, "dtype": "int8", "shape": [6]},               # not a scale type
+        {"offset": 48, "dtype": "float16", "shape": [5]},            # not one per column
+        {"offset": 48, "dtype": "float16", "shape": [6], "block": 2},
+        {"offset": 48, "dtype": "float16", "shape": [2, 6], "block": 2},   # 2 blocks of 2 rows != 6 rows
+        {"offset": 48, "dtype": "float16", "shape": [1, 1, 6]},
+    ]
+    for s in bad_scales:
+        with pytest.raises(MapError) as e:
+            open_with(quantized_entry(scale=s))
+        assert e.value.kind == "bad_header", s
+    m = open_with(quantized_entry(nbytes=84, scale={"offset": 48, "dtype": "float16", "shape": [3, 6], "block": 2}))
+    assert m.tensor("w").scale.layout == "blocks"
+    m.close()
+    t = open_with(quantized_entry(nbytes=52, scale={"offset": 48, "dtype": "float32", "shape": []})).tensor("w")
+    assert t.scale.layout == "tensor"
+    with pytest.raises(MapError):  # a scale on a 16-bit tensor
+        open_with({"offset": 256, "bytes": 8, "shape": [4], "dtype": "bfloat16",
+                   "scale": {"offset": 0, "dtype": "float32", "shape": []}})
+
+
+def test_rotations_are_checked(tmp_path):
+    def open_with(entry):
+        data = bytes(entry["bytes"])
+        return Artifact(hand_map(tmp_path, {"page": 16, "tensors": {"w": entry}}, raw_data=data))
+
+    k, n = 256, 4
+    ok = quantized_entry(nbytes=k * n + 16, shape=(k, n), scale={"offset": k * n, "dtype": "float32", "shape": [n]},
+                         rotation={"kind": "convrot", "group": 256})
+    assert open_with(ok).tensor("w").rotation == artifact.Rotation("convrot", 256)
+    for rotation in ({"kind": "hadamard", "group": 256}, {"kind": "convrot", "group": 128},
+                     {"kind": "convrot", "group": 1024}, {"kind": "convrot"}):
+        with pytest.raises(MapError) as e:
+            open_with(dict(ok, rotation=rotation))
+        assert e.value.kind == "bad_header"
+    with pytest.raises(MapError):  # convrot is int8 only
+        open_with(dict(ok, dtype="float8_e4m3"))
+    with pytest.raises(MapError):  # K not a multiple of the group
+        open_with(quantized_entry(nbytes=320 * n + 16, shape=(320, n),
+                                  scale={"offset": 320 * n, "dtype": "float32", "shape": [n]},
+                                  rotation={"kind": "convrot", "group": 256}))
+
+
+def test_a_published_linear_forges_to_the_maps_layout(tmp_path):
+    """QuantizedMapTests.swift:149-216: N = K = 6, so 36 values, 12 bytes of padding, then the scales."""
+    rng = np.random.default_rng(0)
+    n, k = 6, 6
+    cases = [("int8", "bfloat16", (n, 1)), ("int8", "float32", (n, 1)), ("float8_e4m3", "float32", ()),
+             ("int8", "float16", ())]
+    tensors, published = [], {}
+    for i, (dtype, st, sshape) in enumerate(cases):
+        q = rng.integers(0, 256, (n, k), dtype=np.uint16).astype(np.uint8)
+        if st == "bfloat16":
+            s = rng.integers(0x3C00, 0x3D00, sshape, dtype=np.uint16)
+        else:
+            s = (np.abs(rng.standard_normal(sshape)) * 1e-2 + 1e-3).astype(np.float32 if st == "float32" else np.float16)
+        name = f"layers.0.l{i}.weight"
+        tensors.append(artifact.forge_linear(name, q, s, dtype, st))
+        published[name] = (q, s, dtype, st)
+    bias = np.arange(n, dtype=np.float32)
+    tensors.append(MapTensor("layers.0.l0.bias", "float32", (n,), bias))
+    path = str(tmp_path / "forged.silicon")
+    size = artifact.write_map(path, tensors, header={"kind": "test"})
+    assert size == os.path.getsize(path)
+    with Artifact(path) as m:
+        assert m.linear_weights_transposed and m.header["kind"] == "test"
+        assert m.order == [t.name for t in tensors]
+        assert m.quantized_names() == [t.name for t in tensors[:4]]
+        data_start = m.header["data_start"]
+        assert data_start % artifact.PAGE == 0
+        for name, (q, s, dtype, st) in published.items():
+            t = m.tensor(name)
+            assert t.offset % artifact.PAGE == 0 and t.offset >= data_start
+            assert (t.dtype, t.shape) == (dtype, (k, n))
+            assert t.scale.offset == 48, "36 values, then 12 bytes of padding, then the scales"
+            assert t.scale.dtype == st and t.scale.shape == ((n,) if s.size == n else ())
+            assert np.array_equal(m.values(name), q.T), "the published bytes, transposed"
+            got_type, got = m.scale_values(name)
+            assert got_type == st and got.tobytes() == np.ascontiguousarray(s).tobytes(), "the scales, in their type"
+            assert not m.raw(name)[k * n:48].any()
+        assert m.array("layers.0.l0.bias").tolist() == bias.tolist()
+        assert Artifact.read_header(path) == m.header
+
+
+def test_sq_and_packed_tensors_are_sized(tmp_path):
+    k, n = 256, 3
+    sq = MapTensor("sq", "sq4", (k, n), bytes(n * artifact.sq_row_bytes(k, 4)), np.ones(n, np.float32), "float32", (n,),
+                   rotation=256)
+    q8 = MapTensor("q8", "q4_0", (64, 2), bytes(64 * 2 // 32 * 18))
+    path = str(tmp_path / "packed.silicon")
+    artifact.write_map(path, [sq, q8])
+    with Artifact(path) as m:
+        assert m.tensor("sq").bytes == (n * (128 + 16) + 15) // 16 * 16 + 4 * n
+        assert m.tensor("q8").bytes == 72
+        assert m.quantized_names() == []
