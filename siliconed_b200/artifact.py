@@ -386,6 +386,46 @@ class Artifact:
             raise MapError("bad_header", f"{name}: {t.dtype} has no plain array", self.path)
         return np.frombuffer(self._mm, dtype=np_type, count=t.count, offset=t.offset).reshape(t.shape)
 
+    def materialize(self, name: str, out, ctx=None) -> int:
+        """The tensor's values as fp32 into ``out`` (a float32 numpy array or torch tensor, at least its
+        count long); returns the count (Artifact.materialize, Artifact.swift:670-715).  A tensor larger
+        than ``out`` is refused before a value is written (``does_not_fit``).  bf16 / fp16 / fp32 widen
+        exactly on the host; an 8-bit linear is dequantized by the library on ``ctx``'s device
+        (sc_dequantize: ``float(q) * s``, its convrot applied), so ``ctx`` is required for one."""
+        t = self.tensor(name)
+        contiguous = out.is_contiguous() if hasattr(out, "is_contiguous") else out.flags.c_contiguous
+        if not contiguous or str(out.dtype) not in ("float32", "torch.float32"):
+            raise SiliconedError(abi.INVALID_ARG, f"{name}: the destination must be a contiguous float32 buffer")
+        capacity = int(np.prod(out.shape)) if len(out.shape) else 1
+        if t.count > capacity:
+            raise MapError("does_not_fit", f"{name}: {t.count} values for a buffer of {capacity} - "
+                                           "not the map this model reads", self.path)
+        if t.dtype in ("float32", "float16", "bfloat16"):
+            a = self.array(name).reshape(-1)
+            vals = (a.astype(np.uint32) << 16).view(np.float32) if t.dtype == "bfloat16" else a.astype(np.float32)
+            flat = out.reshape(-1)
+            if hasattr(flat, "copy_"):  # a torch tensor
+                import torch
+                flat[: t.count].copy_(torch.from_numpy(np.ascontiguousarray(vals)))
+            else:
+                flat[: t.count] = vals
+            return t.count
+        if not t.is_quantized or len(t.shape) != 2:
+            raise SiliconedError(abi.UNSUPPORTED_SHAPE, f"{self.path}: {name}: {t.dtype} is not read here")
+        if ctx is None:
+            raise SiliconedError(abi.INVALID_ARG, f"{name}: an 8-bit tensor is dequantized on a device: pass ctx")
+        w = self.register(ctx, name)
+        try:
+            dense = w.dequantize()
+            flat = out.reshape(-1)
+            if hasattr(flat, "copy_"):
+                flat[: t.count].copy_(dense.reshape(-1))
+            else:
+                flat[: t.count] = dense.reshape(-1).cpu().numpy()
+        finally:
+            w.close()
+        return t.count
+
     def register(self, ctx, name: str, **kw):
         """The 8-bit linear ``name`` as a ``QuantizedWeight`` on ``ctx``: its ``[K, N]`` codes and its scale
         read in place (WeightProducts.inPlaceInt8, WeightProducts.swift:855-861), its convrot group

@@ -227,3 +227,32 @@ def test_sq_and_packed_tensors_are_sized(tmp_path):
         assert m.tensor("sq").bytes == (n * (128 + 16) + 15) // 16 * 16 + 4 * n
         assert m.tensor("q8").bytes == 72
         assert m.quantized_names() == []
+
+
+def test_a_tensor_larger_than_its_destination_is_refused_before_writing(tmp_path):
+    """RobustnessTests.swift:116-131: refused (does_not_fit, a damaged map) and not a value lands."""
+    path = hand_map(tmp_path, header())
+    with Artifact(path) as m:
+        out = np.full(3, -7, np.float32)
+        with pytest.raises(MapError) as e:
+            m.materialize("w", out)
+        assert e.value.kind == "does_not_fit" and e.value.path == path
+        assert out.tolist() == [-7, -7, -7], "nothing written"
+        out = np.zeros(5, np.float32)
+        assert m.materialize("w", out) == 4
+        assert out.tolist() == [1, 2, 3, 4, 0]
+
+
+def test_sixteen_bit_tensors_materialize_exactly(tmp_path):
+    bits = np.array([0x3F80, 0xBF81, 0x7F80, 0x0001], np.uint16)   # 1, -1.0078125, +inf, the smallest subnormal
+    halves = np.array([1.0, -2.5, 65504.0, 2.0 ** -24], np.float16)
+    path = str(tmp_path / "sixteen.silicon")
+    artifact.write_map(path, [MapTensor("b", "bfloat16", (4,), bits), MapTensor("h", "float16", (2, 2), halves)])
+    with Artifact(path) as m:
+        out = np.empty(4, np.float32)
+        m.materialize("b", out)
+        assert out.view(np.uint32).tolist() == (bits.astype(np.uint32) << 16).tolist()
+        m.materialize("h", out)
+        assert out.tolist() == halves.astype(np.float32).tolist()
+        with pytest.raises(Exception):
+            m.materialize("h", np.empty(4, np.float64))   # the destination is fp32

@@ -80,6 +80,14 @@ def test_a_forged_map_registers_in_place(ctx, tmp_path):
         got = products.weights[name].dequantize().cpu().numpy()
         assert np.array_equal(canonical(got), canonical(ref)), name
     assert products.weights["d.weight"].rotation == 256
+    # materialize: the same bits into a caller's fp32 buffer, host or device
+    for name in ("a.weight", "d.weight"):
+        out = np.full(want[name].size + 3, -7, np.float32)
+        assert m.materialize(name, out, ctx=ctx) == want[name].size
+        assert np.array_equal(canonical(out[:-3]), canonical(want[name].reshape(-1))) and (out[-3:] == -7).all()
+    out = torch.empty(want["b.weight"].size, dtype=torch.float32, device="cuda")
+    m.materialize("b.weight", out, ctx=ctx)
+    assert np.array_equal(canonical(out.cpu().numpy()), canonical(want["b.weight"].reshape(-1)))
 
     # the products: the same bits as the weight registered from the arrays
     direct = {
