@@ -555,22 +555,57 @@ def write_map(path: str, tensors: list[MapTensor], header: dict | None = None, p
     return begin + end
 
 
-def forge_linear(name: str, values_nk: np.ndarray, scales: np.ndarray, dtype: str, scale_dtype: str,
+class ForgeRefusal(ValueError):
+    """A published 8-bit weight the forge does not keep, with the reason (the reference's forge refusals,
+    QuantizedMapTests.swift:485-503, 620-641)."""
+
+
+def _scale_as_f32(s: np.ndarray, scale_dtype: str) -> np.ndarray:
+    if scale_dtype == "bfloat16":
+        return (s.astype(np.uint32) << 16).view(np.float32)
+    return s.astype(np.float32)
+
+
+def forge_linear(name: str, values_nk: np.ndarray, scales: np.ndarray | None, dtype: str, scale_dtype: str | None,
                  rotation: int | None = None) -> MapTensor:
     """A published 8-bit ``nn.Linear`` weight as the map keeps it (the forge's ``kept8bit`` outcome,
     QuantizedMapTests.swift:149-216): the codes ``[N, K]`` transposed to ``[K, N]`` byte for byte, the
     scale (``[N, 1]`` / ``[N]`` per output row, or ``[]`` / ``[1]`` for the tensor) kept in its published
-    type and flattened to ``[N]`` or ``[]``.  ``scales`` holds bf16 as uint16 bits."""
-    if dtype not in ("int8", "float8_e4m3") or scale_dtype not in SCALE_TYPES:
-        raise ValueError(f"{name}: {dtype} with a {scale_dtype} scale")
+    type and flattened to ``[N]`` or ``[]``.  ``scales`` holds bf16 as uint16 bits.
+
+    Refused (``ForgeRefusal``), as the forge does: an int8 weight without a scale (an fp8 one without a
+    scale is a plain cast, w = f8); a scale shaped otherwise than one per tensor or one per row; a nonzero
+    scale whose smallest product ``|s| * min|q| / sqrt(G)`` is subnormal in fp32 (min|q| = 1 for int8,
+    2^-9 for e4m3; ``QuantizedLayouts.checkSubnormal``, Forge/Quantization.swift:380-402)."""
+    if dtype not in ("int8", "float8_e4m3"):
+        raise ForgeRefusal(f"{name}: {dtype} is not an 8-bit weight type")
     q = np.ascontiguousarray(values_nk).view(np.uint8)
+    if q.ndim != 2:
+        raise ForgeRefusal(f"{name}: a linear weight is [N, K], not {list(q.shape)}")
     n, k = q.shape
+    if scales is None:
+        if dtype == "int8":
+            raise ForgeRefusal(f"{name}: int8 without a scale")
+        if rotation:
+            raise ForgeRefusal(f"{name}: a rotation needs a scale")
+        return MapTensor(name, dtype, (k, n), np.ascontiguousarray(q.T), transposed=True)
+    if scale_dtype not in SCALE_TYPES:
+        raise ForgeRefusal(f"{name}: a scale of type {scale_dtype}")
     s = np.ascontiguousarray(scales)
-    if s.size == 1:
+    if s.shape in ((), (1,)):
         s_shape: tuple[int, ...] = ()
-    elif s.size == n:
+    elif s.shape in ((n,), (n, 1)):
         s_shape = (n,)
     else:
-        raise ValueError(f"{name}: {s.size} scales for {n} outputs")
+        raise ForgeRefusal(f"{name}: a scale {list(s.shape)} for [{n}, {k}]: only one per tensor or one per row")
+    # in fp32, as the forge computes it (a product rounded to the nearest subnormal can reach 2^-126)
+    smallest = np.float32((1.0 if dtype == "int8" else 2.0 ** -9) / np.sqrt(float(rotation or 1)))
+    sf = np.abs(_scale_as_f32(s.reshape(-1), scale_dtype))
+    with np.errstate(under="ignore"):
+        low = (sf != 0) & (sf * smallest < np.float32(2.0 ** -126))
+    if np.any(low):
+        raise ForgeRefusal(f"{name}: a scale whose products can fall below 2^-126 (subnormal)")
+    if rotation and (dtype != "int8" or not is_rotation_group(rotation) or k % rotation != 0):
+        raise ForgeRefusal(f"{name}: rotation convrot of group {rotation} on {dtype} [{n}, {k}]")
     return MapTensor(name, dtype, (k, n), np.ascontiguousarray(q.T), s.reshape(s_shape), scale_dtype, s_shape,
                      rotation=rotation, transposed=True)

@@ -256,3 +256,32 @@ def test_sixteen_bit_tensors_materialize_exactly(tmp_path):
         assert out.tolist() == halves.astype(np.float32).tolist()
         with pytest.raises(Exception):
             m.materialize("h", np.empty(4, np.float64))   # the destination is fp32
+
+
+def test_the_forge_refuses_what_the_reference_refuses():
+    """QuantizedMapTests.swift:485-503, 620-641: int8 without a scale, a scale neither per tensor nor per
+    row, subnormal products (1e-39 for int8; 2^-120 fine for int8 but not for e4m3); an fp8 weight
+    without a scale is a plain cast."""
+    q = np.arange(8, dtype=np.uint8).reshape(2, 4)
+    with pytest.raises(artifact.ForgeRefusal, match="without a scale"):
+        artifact.forge_linear("a.weight", q, None, "int8", None)
+    with pytest.raises(artifact.ForgeRefusal, match="only one per tensor or one per row"):
+        artifact.forge_linear("a.weight", q, np.zeros((2, 2), np.float32), "int8", "float32")
+    with pytest.raises(artifact.ForgeRefusal, match="only one per tensor or one per row"):
+        artifact.forge_linear("a.weight", np.zeros((4, 4), np.uint8), np.ones((1, 4), np.float32), "int8", "float32")
+    with pytest.raises(artifact.ForgeRefusal, match="subnormal"):
+        artifact.forge_linear("a.weight", q, np.array(1e-39, np.float32), "int8", "float32")
+    small = np.array(2.0 ** -120, np.float32)
+    assert artifact.forge_linear("a.weight", q, small, "int8", "float32").scale_shape == ()
+    with pytest.raises(artifact.ForgeRefusal, match="subnormal"):
+        artifact.forge_linear("a.weight", q, small, "float8_e4m3", "float32")
+    # rotated: the smallest product is |s| / sqrt(G)
+    q256 = np.zeros((2, 256), np.uint8)
+    with pytest.raises(artifact.ForgeRefusal, match="subnormal"):
+        artifact.forge_linear("a.weight", q256, np.array(2.0 ** -123, np.float32), "int8", "float32", rotation=256)
+    with pytest.raises(artifact.ForgeRefusal, match="rotation"):
+        artifact.forge_linear("a.weight", q, np.ones(2, np.float32), "int8", "float32", rotation=256)
+    # zero scales are not refused; an fp8 weight without a scale is a plain cast
+    assert artifact.forge_linear("a.weight", q, np.zeros(2, np.float32), "int8", "float32").scale_shape == (2,)
+    cast = artifact.forge_linear("c.weight", q, None, "float8_e4m3", None)
+    assert cast.scale is None and cast.shape == (4, 2) and cast.total_bytes() == 8
