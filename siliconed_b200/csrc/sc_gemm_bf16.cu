@@ -176,8 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (i < n0) {
           uint4 lo, hi;
           codes16_to_bf16<kFW == 1 ? 1 : 2, kFW == 3>(in[u], lo, hi);
-          fw.out[2 * i] = lo;
-          fw.out[2 * i + 1] = hi;
+          st_global_32b(fw.out + 2 * i, lo, hi);
         }
       }
     }
@@ -294,12 +293,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint4 in1 = i1 < c1 ? __ldcs(fw.codes + i1) : make_uint4(0, 0, 0, 0);
         uint4 lo, hi;
         codes16_to_bf16<kFW == 1 ? 1 : 2, kFW == 3>(in0, lo, hi);
-        fw.out[2 * base] = lo;
-        fw.out[2 * base + 1] = hi;
+        st_global_32b(fw.out + 2 * base, lo, hi);
         if (i1 < c1) {
           codes16_to_bf16<kFW == 1 ? 1 : 2, kFW == 3>(in1, lo, hi);
-          fw.out[2 * i1] = lo;
-          fw.out[2 * i1 + 1] = hi;
+          st_global_32b(fw.out + 2 * i1, lo, hi);
         }
       }
       named_barrier_sync(2, kThreads - 64);
@@ -663,8 +660,7 @@ __global__ void __launch_bounds__(256) widen_codes(const uint4* __restrict__ cod
     if (i < chunks) {
       uint4 lo, hi;
       codes16_to_bf16<kKind, kNaN>(in[u], lo, hi);
-      out[2 * i] = lo;
-      out[2 * i + 1] = hi;
+      st_global_32b(out + 2 * i, lo, hi);
     }
   }
 }

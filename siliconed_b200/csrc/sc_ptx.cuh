@@ -139,6 +139,20 @@ __device__ __forceinline__ void multimem_st_v4(void* mc, uint4 v) {
                : "memory");
 }
 
+// Two 16-byte values to 32 contiguous bytes of global memory: one 256-bit store (st.global.v8.b32,
+// sm_100) when the address is 32-byte aligned, so that a warp's store covers whole 32-byte sectors in
+// one instruction; two 128-bit stores otherwise.
+__device__ __forceinline__ void st_global_32b(uint4* p, uint4 lo, uint4 hi) {
+  if ((reinterpret_cast<uintptr_t>(p) & 31u) == 0) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(lo.x), "r"(lo.y),
+                 "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
+                 : "memory");
+  } else {
+    p[0] = lo;
+    p[1] = hi;
+  }
+}
+
 // 16-byte global load cached in L2 only (data this kernel also writes: not the read-only path).
 __device__ __forceinline__ float4 ld_cg_f4(const float* p) {
   float4 v;
