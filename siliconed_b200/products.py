@@ -389,7 +389,7 @@ class WeightProducts:
         A weight ``<base>.weight`` takes the map's ``<base>.bias`` when it is a bf16 vector of N values,
         as a device tensor; any other bias stays the caller's to give.  Returns the names registered."""
         names = artifact.quantized_names() if names is None else list(names)
-        device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        device = torch.device("cuda", self.ctx.device) if device is None else device
         for name in names:
             w = artifact.register(self.ctx, name)
             self.weights[name] = w
