@@ -4,12 +4,15 @@ Default workload (config 1 of the benchmark configs, the one the headline metric
 one int8 weight-only linear, x bf16 [4096, 3072], W int8 [3072, 3072] per-output-channel scales,
 bf16 bias, fp32 accumulation, bf16 output.  A step is one product over that batch.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg1|cfg2|gemv1|gemv4|gemv16|gemv32]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg1|cfg2|gemv1|gemv4|gemv16|gemv32|...]
   python bench.py --impl reference ...   # the reference's CPU path (the oracle), on the host cores
 
-With N > 1 (one process per GPU under torch.distributed.run) every rank runs its own batch of the
-workload with the weight replicated (batch sharding: the images / token batches are independent, no
-collective on the data path); ``value`` is the work of all ranks over the slowest rank's time.
+With N > 1 (one process per GPU under torch.distributed.run) config 1 runs column-parallel: rank r
+multiplies x by its block of W's columns and the product's epilogue stores every output tile into every
+rank's y over NVLink, so each rank ends the step holding the whole y (strong scaling; ``run_scale``,
+with a bit-exact check against one GPU's product before timing).  ``--workload cfg1-replicas`` (and
+the other workloads) give every rank its own batch with the weight replicated instead (batch sharding,
+no collective on the data path); ``value`` is the work of all ranks over the slowest rank's time.
 Timing: W untimed warm-up steps, then K timed steps, each bracketed by CUDA events on the launching
 stream, with the L2 flushed (a 256 MiB write, then a 256 MiB read of another buffer so that the L2
 holds clean lines) before every step; barrier + synchronize around the
@@ -46,7 +49,7 @@ def load_peaks():
 
 def make_case(workload: str):
     from siliconed_b200 import configs
-    if workload in ("cfg1", "cfg1-w8a8"):
+    if workload in ("cfg1", "cfg1-w8a8", "cfg1-replicas"):
         return configs.config1()
     if workload == "cfg2":
         return configs.config2()
@@ -56,12 +59,24 @@ def make_case(workload: str):
     raise SystemExit(f"unknown workload {workload}")
 
 
-def describe(case, workload):
+def parallelism_of(workload: str, world: int) -> str:
+    """How N > 1 GPUs share a step: config 1 (the default) splits W's columns over the ranks and gathers y
+    inside the product (strong scaling); `cfg1-replicas` and the GEMV workloads give every rank a whole
+    product (weak scaling)."""
+    if world <= 1:
+        return "one GPU"
+    if workload == "cfg1":
+        return f"column-parallel x{world}: W's columns split over the ranks, y gathered in the product's epilogue"
+    return f"replicas x{world} (batch-sharded)"
+
+
+def describe(case, workload, world=1):
     bound = "hbm" if case.m <= 32 else "tensor"
     return {"workload": f"{workload}: {case.name} x bf16 [{case.m}, {case.k}] . W [{case.k}, {case.n}] "
                         f"{'int8' if case.kind == 1 else 'e4m3'} per-channel, fp32 accumulate, bf16 out",
             "m": case.m, "k": case.k, "n": case.n, "bias": case.bias is not None, "bound": bound,
-            "l2": "flushed before every timed step (256 MiB write, then a 256 MiB read that leaves the L2 clean)"}
+            "l2": "flushed before every timed step (256 MiB write, then a 256 MiB read that leaves the L2 clean)",
+            "parallelism": parallelism_of(workload, world)}
 
 
 def metric_of(case):
@@ -194,10 +209,12 @@ def run_reference(args):
     value = (byts / per / 1e9) if unit == "GB/s" else (flops / per / 1e12)
     sample = (f"{rows} of {case.m} rows per step ({reps} steps timed after {args.warmup} untimed), full weight "
               f"dequantized each step (oracle/ C, OpenMP) + fp32 torch.matmul on the CPU")
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
             "steps": reps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": describe(case, args.workload),
+            "scaling": "strong" if (world > 1 and args.workload == "cfg1") else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": describe(case, args.workload, world),
             "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -338,7 +355,7 @@ def run_ours(args):
         line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "int8" if w8a8 else "bf16", "data": "synthetic",
-                "config": dict(describe(case, args.workload), parallelism=f"replicas x{world} (batch-sharded)"),
+                "config": describe(case, args.workload, world),
                 "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": runit,
                              "frac": achieved / peak, "traffic": traffic,
                              "peak_source": f"{peak_src} (burst figure: the kernel is timed alone)",
@@ -368,6 +385,162 @@ def run_ours(args):
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
+    return 0
+
+
+def run_scale(args):
+    """Config 1 on N > 1 GPUs, the default workload there (strong scaling: the total work is config 1's one
+    product whatever N is).  Rank r registers W's columns column_ranges(N, P)[r] and multiplies the whole x
+    by them; the product's epilogue stores every output tile into every rank's y over NVLink and raises an
+    epoch flag on each rank, and a bounded wait kernel holds each rank's stream until all columns have
+    landed (FusedColumnParallelLinear, sc_linear_allgather).  A step is one such call: widen, gathering GEMM,
+    wait.  Before timing, every rank checks its gathered y against a single-GPU product of the whole weight,
+    bit for bit ("parity").  The stores go to the peers' outputs opened through CUDA IPC; --multicast sends
+    one multimem store per piece to the outputs' NVLink multicast address instead (torch symmetric memory).
+    value: 77.31 GFLOP over the slowest rank's time per step."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from siliconed_b200 import configs, parallel
+    from siliconed_b200.products import Context, QuantizedWeight
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    case = configs.config1()
+    metric, unit = metric_of(case)
+    ctx = Context(local)
+    x = torch.from_numpy(case.x.view(np.int16)).cuda().view(torch.bfloat16)
+    bias = torch.from_numpy(case.bias.view(np.int16)).cuda().view(torch.bfloat16)
+    fused = parallel.FusedColumnParallelLinear(ctx, case.codes_nk, case.kind, case.scales, case.n, case.m,
+                                               published_nk=True, bias=bias, multicast=args.multicast)
+    stream = torch.cuda.current_stream()
+
+    # parity, once: the gathered y of every rank against one GPU's product of the whole weight
+    full = QuantizedWeight(ctx, case.codes_nk, case.kind, case.scales, published_nk=True)
+    ws_full = torch.empty(max(full.workspace_bytes(case.m), 1), dtype=torch.uint8, device="cuda")
+    y_ref = full.linear(x, bias=bias, workspace=ws_full)
+    y_got = fused(x).clone()
+    torch.cuda.synchronize()
+    ctx.poll_errors()
+    same = torch.tensor([1 if torch.equal(y_got.view(torch.int16), y_ref.view(torch.int16)) else 0],
+                        dtype=torch.int32, device="cuda")
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    parity = bool(same.item() == 1)
+    full.close()
+    del y_ref, y_got, ws_full
+
+    y_local = torch.empty((case.m, fused.n1 - fused.n0), dtype=torch.bfloat16, device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    clean = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
+
+    def flush_l2(i):
+        flush.fill_(i & 0xFF)
+        torch.sum(clean, dim=0, out=sink)
+
+    def step():
+        fused(x)
+
+    def product_alone():
+        fused.w.linear(x, bias=fused.bias, out=y_local, workspace=fused.ws, stream=stream)
+
+    def timed(fn, clocks=None):
+        for i in range(args.warmup):
+            flush_l2(1)
+            fn()
+        torch.cuda.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        dist.barrier()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(int(2e6) * max(1, args.steps // 10))
+        for i in range(args.steps):
+            flush_l2(i)
+            starts[i].record(stream)
+            fn()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        per = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+        t = torch.tensor([sum(per)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()) / args.steps, per
+
+    with ClockSampler(local) as clocks:
+        ms_step, per_step = timed(step)
+    ms_alone, _ = timed(product_alone)
+    ctx.poll_errors()
+
+    # End to end through the public call: x from pinned host memory, the fused product and gather, y back.
+    x_host = torch.from_numpy(case.x.view(np.int16)).view(torch.bfloat16).pin_memory()
+    y_host = torch.empty((case.m, case.n), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y = fused(x_dev)
+        y_host.copy_(y, non_blocking=True)
+    for _ in range(2):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 20))
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    dist.barrier()
+    ctx.poll_errors()
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        value = case.flops / (ms_step / 1e3) / 1e12
+        width = max(b - a for a, b in fused.ranges)
+        bytes_in = case.m * (case.n - width) * 2             # y's columns that arrive from the other ranks
+        nvlink_gbs = 770.0                                   # measured peer copy per direction per GPU
+        t_tensor = case.flops / world / (peaks["bf16_tflops"] * 1e12)
+        t_link = bytes_in / (nvlink_gbs * 1e9)
+        target_ms = 1e3 * max(t_tensor, t_link)
+        line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": describe(case, args.workload, world),
+                "parity": parity,
+                "parity_check": "before timing, every rank's gathered y [4096, 3072] equal bit for bit to one "
+                                "GPU's product of the whole weight",
+                "collective": {"path": ("multicast stores (multimem.st to the outputs' NVLink multicast address)"
+                                        if fused.uses_multicast else "peer stores over NVLink (CUDA IPC)"),
+                               "columns_per_rank": width, "product_alone_us": ms_alone * 1e3,
+                               "with_gather_us": ms_step * 1e3, "gather_extra_us": (ms_step - ms_alone) * 1e3,
+                               "bytes_into_each_gpu": bytes_in,
+                               "gb_s_into_each_gpu": bytes_in / (ms_step / 1e3) / 1e9},
+                "roofline": {"bound": "tensor" if t_tensor >= t_link else "nvlink",
+                             "achieved": value / world, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": value / world / peaks["bf16_tflops"], "traffic": None,
+                             "peak_source": f"{peak_src} (burst figure)",
+                             "fused_target_us": target_ms * 1e3, "frac_of_fused_target": target_ms / ms_step,
+                             "target": "max(FLOPs per GPU / measured bf16 peak, bytes into each GPU / 770 GB/s "
+                                       "measured peer copy)"},
+                "clocks": clocks.summary(),
+                "e2e": {"value": case.flops / (float(te.item()) / 1e3 / e2e_steps) / 1e12, "unit": unit,
+                        "h2d_bytes_per_step": int(case.x.nbytes), "d2h_bytes_per_step": int(case.m * case.n * 2),
+                        "path": "FusedColumnParallelLinear (sc_linear_allgather + sc_allgather_wait) with x copied "
+                                "in from pinned host memory and the gathered y copied back, every step, every rank"},
+                "gpu_launches": args.steps * 3,
+                "step_ms_min": min(per_step), "step_ms_median": statistics.median(per_step)}
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    fused.close()
+    ctx.close()
+    dist.destroy_process_group()
     return 0
 
 
@@ -710,11 +883,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="cfg1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--multicast", action="store_true",
+                    help="N > 1: the gathered stores go to an NVLink multicast address (default: peer stores)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.workload == "cfg1-colpar" and args.impl == "ours":
         return run_colpar(args)
+    if args.workload == "cfg1" and args.impl == "ours" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        return run_scale(args)
     if args.workload in DIT_WORKLOADS:
         if args.impl == "reference":
             rank = int(os.environ.get("RANK", "0"))

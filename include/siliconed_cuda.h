@@ -15,6 +15,14 @@
  *   - `stream` is a cudaStream_t (NULL = the legacy default stream).  Every compute call is
  *     asynchronous on that stream; sc_sync / sc_poll_errors wait.
  *   - A context is used by one host thread at a time; distinct contexts may run concurrently.
+ *   - Products of one context may run on several streams at once when each has its own workspace
+ *     (and its own x and y).  The one piece of state they share, the readiness counters of the
+ *     widening inside the GEMM (config-1-sized products from 1536 rows), is guarded: a product whose
+ *     stream differs from that of the last product that used them, while that product may still be
+ *     running, takes the separate widening instead (same bits); so does a product issued under
+ *     stream capture.  The counters return to zero at the end of every launch that uses them.
+ *   - Every call selects the context's device as the calling thread's current device and leaves
+ *     it selected.
  *   - The library never falls back to the CPU: without a usable sm_100 device every call fails.
  */
 #ifndef SILICONED_CUDA_H
@@ -267,9 +275,9 @@ SC_API sc_status sc_linear_heads(sc_ctx* ctx, const sc_weight* w, const sc_bf16*
 
 /* sc_linear_ex with its scratch in a 32 MiB device array of the library instead of a workspace: it
  * allocates nothing and takes no workspace argument.  No counterpart in the reference: it serves
- * callers that have no scratch buffer to pass (a binding that keeps the signature of
- * WeightProducts.linear, which carries only a, c, m, k, n) and may not allocate per call
- * (cudaMalloc / cudaFree synchronise the device, which a serving loop cannot afford).  A product
+ * callers that have no scratch buffer to pass (a binding whose linear call carries only the operand,
+ * the output and the sizes) and may not allocate per call (cudaMalloc / cudaFree synchronise the
+ * device, which a serving loop cannot afford).  A product
  * whose sc_workspace_size exceeds 32 MiB (from 1536 rows: n_pad * k_pad * 2 bytes of widened weight)
  * returns SC_UNSUPPORTED_SHAPE.  The first call on a device sets up the array's address
  * (cudaGetSymbolAddress) and should come before any stream capture.  All calls on a device share the

@@ -204,6 +204,40 @@ sc_status rotate_operand(sc_ctx* ctx, const sc_weight* w, const sc_bf16*& x, int
   return SC_OK;
 }
 
+// Whether a product on stream `st` may run the widening inside its GEMM, which uses the context's one set of
+// readiness counters: yes unless the last launch that used them went to another stream and may still be
+// running (then the product takes the separate widening, which gives the same bits and shares nothing).
+// Under stream capture nothing can be asked of an event, and the separate widening is taken.
+sc_status fused_widen_free(sc_ctx* ctx, cudaStream_t st, bool& free) {
+  free = false;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaError_t e = cudaStreamIsCapturing(st, &cap); e != cudaSuccess) return check_cuda(ctx, e, "capture query");
+  if (cap != cudaStreamCaptureStatusNone) return SC_OK;
+  if (ctx->fw_launched && ctx->fw_stream != st) {
+    const cudaError_t e = cudaEventQuery(ctx->fw_event);
+    if (e == cudaErrorNotReady) {
+      cudaGetLastError();
+      return SC_OK;
+    }
+    if (e != cudaSuccess) return check_cuda(ctx, e, "event query");
+  }
+  free = true;
+  return SC_OK;
+}
+
+// Records the stream and completion event of a launch that used the readiness counters.
+sc_status fused_widen_launched(sc_ctx* ctx, cudaStream_t st) {
+  if (ctx->fw_event == nullptr) {
+    sc_status s = check_cuda(ctx, cudaEventCreateWithFlags(&ctx->fw_event, cudaEventDisableTiming), "event");
+    if (s != SC_OK) return s;
+  }
+  sc_status s = check_cuda(ctx, cudaEventRecord(ctx->fw_event, st), "event record");
+  if (s != SC_OK) return s;
+  ctx->fw_stream = st;
+  ctx->fw_launched = true;
+  return SC_OK;
+}
+
 sc_status run_gemv(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, void* y,
                    bool f32_out, void* workspace, size_t workspace_bytes, cudaStream_t st) {
   const size_t need = gemv_workspace_bytes(w, m, ctx->sm_count);
@@ -240,15 +274,16 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
         (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0) {
       CUtensorMap tmw;
       if ((s = make_tmap_widened(ctx, w, workspace, &tmw)) != SC_OK) return s;
-      if (fused_widen_fits(w, m, ctx->sm_count)) {
+      bool fused = false;
+      if (fused_widen_fits(w, m, ctx->sm_count) && (s = fused_widen_free(ctx, st, fused)) != SC_OK) return s;
+      if (fused) {
         // a few rounds of tiles: the GEMM's CTAs widen the codes themselves, the first round's columns
         // first, the rest while the pipeline runs
-        uint32_t* bank = ctx->d_widen + ctx->widen_bank * kWidenBankWords;
-        uint32_t* next = ctx->d_widen + (1 - ctx->widen_bank) * kWidenBankWords;
-        ctx->widen_bank ^= 1;
-        return check_cuda(ctx, launch_gemm_bf16_fw(tmx, tmw, w, bias, y, f32_out, workspace, bank, next, m,
-                                                   ctx->d_err, ctx->sm_count, st),
-                          "bf16 pair gemm (fused widening) launch");
+        if ((s = check_cuda(ctx, launch_gemm_bf16_fw(tmx, tmw, w, bias, y, f32_out, workspace, ctx->d_widen, m,
+                                                     ctx->d_err, ctx->sm_count, st),
+                            "bf16 pair gemm (fused widening) launch")) != SC_OK)
+          return s;
+        return fused_widen_launched(ctx, st);
       }
       if ((s = check_cuda(ctx, launch_widen(w, workspace, ctx->sm_count, st), "widen launch")) != SC_OK) return s;
       return check_cuda(ctx, launch_gemm_bf16(tmx, tmw, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
@@ -318,8 +353,8 @@ sc_status sc_ctx_create(int device, sc_ctx** out) {
   ctx->encode_tiled = reinterpret_cast<sc_encode_tiled_fn>(fn);
   if (cudaMalloc(&ctx->d_err, kCtxWords * sizeof(int)) != cudaSuccess ||
       cudaMemset(ctx->d_err, 0, kCtxWords * sizeof(int)) != cudaSuccess ||
-      cudaMalloc(&ctx->d_widen, 2 * kWidenBankWords * sizeof(uint32_t)) != cudaSuccess ||
-      cudaMemset(ctx->d_widen, 0, 2 * kWidenBankWords * sizeof(uint32_t)) != cudaSuccess) {
+      cudaMalloc(&ctx->d_widen, (kWidenCounterWords + 32) * sizeof(uint32_t)) != cudaSuccess ||
+      cudaMemset(ctx->d_widen, 0, (kWidenCounterWords + 32) * sizeof(uint32_t)) != cudaSuccess) {
     cudaGetLastError();
     if (ctx->d_err) cudaFree(ctx->d_err);
     if (ctx->d_widen) cudaFree(ctx->d_widen);
@@ -337,6 +372,7 @@ void sc_ctx_destroy(sc_ctx* ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->d_widen) cudaFree(ctx->d_widen);
+  if (ctx->fw_event) cudaEventDestroy(ctx->fw_event);
   for (cudaEvent_t e : ctx->host_events)
     if (e) cudaEventDestroy(e);
   if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);

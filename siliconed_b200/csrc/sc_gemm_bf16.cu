@@ -158,8 +158,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // overlapped their end; nothing reads or writes global memory before this point.
   pdl_wait();
   if (kFW != 0) {
-    if (blockIdx.x == 0)
-      for (int i = threadIdx.x; i < fw.n_blocks; i += kThreads) fw.next_bank[i] = 0;
     // every thread of the grid: the first round's column blocks
     const int64_t n0 = static_cast<int64_t>(fw.first_blocks) * fw.chunks_per_block;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
@@ -636,6 +634,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem, kTmemCols);
   }
+  if (kFW != 0 && threadIdx.x == 0) {
+    // Every role of this CTA is done, its producer past its last wait on the counters.  The CTA counts its
+    // exit; the last one to leave returns the counters to zero, so the next launch (stream-ordered after
+    // this one, a graph replay included) starts from zero and no launch depends on another's bookkeeping.
+    __threadfence();
+    if (atomicAdd(fw.done, 1u) == gridDim.x - 1) {
+      __threadfence();
+      for (int b = 0; b < fw.n_blocks; ++b) fw.counters[b] = 0;
+      *fw.done = 0;
+      __threadfence();
+    }
+  }
 }
 
 // Widens the arena's codes [n_pad][k_pad] to bf16 in the same layout.  Each thread takes kPer
@@ -719,7 +729,7 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[3];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -730,6 +740,31 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
+  if (kFW != 0) {
+    // The fused widening's CTAs wait for one another, so they must all be resident at once: asked of the
+    // runtime as a cooperative launch where it takes one beside the cluster shape (tried once per device;
+    // a refused launch is an ordinary error, cleared, and the launch then goes without the attribute,
+    // sized to the co-resident clusters as above).
+    static signed char cooperative[64] = {0};  // 0 untried, 1 accepted, -1 refused
+    int dev = 0;
+    if (cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return e;
+    if (cooperative[dev & 63] >= 0) {
+      attr[2].id = cudaLaunchAttributeCooperative;
+      attr[2].val.cooperative = 1;
+      cfg.numAttrs = 3;
+      const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias,
+                                               y, static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles,
+                                               n_tiles, err, peers, gate, row_scales, ho, xh, fw);
+      if (e == cudaSuccess) {
+        cooperative[dev & 63] = 1;
+        return e;
+      }
+      if (cooperative[dev & 63] == 1) return e;  // accepted before: a real failure
+      cudaGetLastError();
+      cooperative[dev & 63] = -1;
+      cfg.numAttrs = 2;
+    }
+  }
   return cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias, y,
                             static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers, gate,
                             row_scales, ho, xh, fw);
@@ -805,19 +840,19 @@ bool fused_widen_fits(const sc_weight* w, int64_t m, int sm_count) {
   // 10 of 74 us; 70 us with it inside).  With more rounds its share shrinks and the blocks widened during
   // the run fall behind the tiles that need them (config 2, 8.6 rounds: 259 us inside against 233 apart).
   const int64_t tiles = m_tiles * n_tiles, pairs = sm_count / 2;
-  return m_tiles <= kTileGroupRows && tiles >= 2 * pairs && tiles <= 3 * pairs && n_tiles <= kWidenBankWords;
+  return m_tiles <= kTileGroupRows && tiles >= 2 * pairs && tiles <= 3 * pairs && n_tiles <= kWidenCounterWords;
 }
 
 cudaError_t launch_gemm_bf16_fw(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
                                 const uint16_t* bias, void* y, bool f32_out, void* widened, uint32_t* counters,
-                                uint32_t* next_bank, int64_t m, int* err, int sm_count, cudaStream_t stream) {
+                                int64_t m, int* err, int sm_count, cudaStream_t stream) {
   using namespace gemm_bf16;
   const PeerOut none = {};
   FusedWiden fw;
   fw.codes = reinterpret_cast<const uint4*>(w->values);
   fw.out = static_cast<uint4*>(widened);
   fw.counters = counters;
-  fw.next_bank = next_bank;
+  fw.done = counters + kWidenCounterWords;
   fw.chunks_per_block = static_cast<int>(BN * w->k_pad / 16);
   fw.n_blocks = static_cast<int>(w->n_pad / BN);
   fw.first_blocks = 0;  // set by launch_gemm from the pairs it launches

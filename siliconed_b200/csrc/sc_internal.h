@@ -47,10 +47,14 @@ struct sc_ctx {
                          // fused gather's CTA counter (zero between launches)
   sc_encode_tiled_fn encode_tiled = nullptr;
   std::string last_error;
-  // The fused widening's readiness counters: two banks of kWidenBankWords, zeroed at creation; calls
-  // alternate banks (each call zeroes the other one for the next).
+  // The fused widening's readiness counters (kWidenCounterWords, then the CTA exit count), zeroed at
+  // creation; every launch that uses them returns them to zero as its last CTA leaves.
   uint32_t* d_widen = nullptr;
-  int widen_bank = 0;
+  // The stream of the last launch that used them and an event recorded after it: a product on another
+  // stream that would use them while that launch may still run takes the separate widening instead.
+  cudaStream_t fw_stream = nullptr;
+  cudaEvent_t fw_event = nullptr;
+  bool fw_launched = false;
   // sc_linear_host's copy streams and events, created on its first call and kept with the context.
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
   cudaEvent_t host_events[2 * 32 + 2] = {};
@@ -137,20 +141,20 @@ struct HeadOut {
 // plain [M, K] matrix.
 // The widening done inside the bf16 pair GEMM (launch_gemm_bf16_fw): codes -> the workspace's bf16 copy
 // by the GEMM's own CTAs, column block by column block, each block's readiness counted in counters[block]
-// (this call's bank, zero at launch; the kernel zeroes next_bank for the next call).
+// (zero at launch; the last CTA to leave zeroes them and `done`, its count of CTAs that left).
 struct FusedWiden {
   const uint4* codes;
   uint4* out;
   uint32_t* counters;
-  uint32_t* next_bank;
+  uint32_t* done;
   int chunks_per_block;  // 256 * k_pad / 16: 16-code chunks of one 256-column block
   int first_blocks;      // the blocks the first round of tiles reads, widened by every thread first
   int n_blocks;          // n_pad / 256
 };
-constexpr int kWidenBankWords = 1024;  // column blocks per counter bank (N up to 262144)
+constexpr int kWidenCounterWords = 1024;  // column blocks with a counter (N up to 262144)
 cudaError_t launch_gemm_bf16_fw(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const sc_weight* w,
                                 const uint16_t* bias, void* y, bool f32_out, void* widened, uint32_t* counters,
-                                uint32_t* next_bank, int64_t m, int* err, int sm_count, cudaStream_t stream);
+                                int64_t m, int* err, int sm_count, cudaStream_t stream);
 // Whether launch_gemm_bf16_fw serves a product of m rows: two to three rounds of pair tiles, one group of
 // the tile order (m_tiles <= 16).
 bool fused_widen_fits(const sc_weight* w, int64_t m, int sm_count);

@@ -444,6 +444,35 @@ def test_rows_do_not_depend_on_the_batch(ctx):
     w.close()
 
 
+def test_products_on_two_streams_at_once(ctx):
+    """Two products of one context in flight at once on two streams, each with its own workspace, both
+    of config 1's shape (whose tiles take the widening inside the GEMM, with the context's readiness
+    counters): every output has the bits of the same product run alone, over alternating calls."""
+    g = np.random.default_rng(17)
+    m, k, n = 4096, 3072, 3072
+    q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+    s = (np.abs(g.standard_normal(n)) * 0.02 / 127 + 1e-6).astype(np.float32)
+    w = QuantizedWeight(ctx, q, abi.WEIGHT_INT8, s)
+    xs = [bf16_dev(configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))) for _ in range(2)]
+    refs = [bf16_host(linear_ex(ctx, w, x, m, None, False)) for x in xs]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    wss = [torch.empty(w.workspace_bytes(m), dtype=torch.uint8, device="cuda") for _ in range(2)]
+    torch.cuda.synchronize()
+    outs = []
+    for call in range(6):
+        i = call % 2
+        with torch.cuda.stream(streams[i]):
+            torch.cuda._sleep(200000)              # keeps this stream's product in flight while the next is issued
+            y = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+            w.linear(xs[i], out=y, workspace=wss[i], stream=streams[i])
+            outs.append((i, y))
+    torch.cuda.synchronize()
+    ctx.poll_errors()
+    for call, (i, y) in enumerate(outs):
+        assert np.array_equal(bf16_host(y), refs[i]), call
+    w.close()
+
+
 # ---------------------------------------------------------------------------------------------
 # the benchmark configs at full size: sampled rows against fp32 CPU products
 

@@ -30,6 +30,7 @@ def _worker(rank, world, port, results, multicast=False):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
+    ctx = fused = full = None
     try:
         ctx = Context(rank)
         case = configs.config1(m=1600, k=512, n=1000)
@@ -49,10 +50,18 @@ def _worker(rank, world, port, results, multicast=False):
             ctx.poll_errors()
             ok &= bool(torch.equal(y.view(torch.int16), ref.view(torch.int16)))
         results[rank] = ok
-        fused.close()
-        full.close()
         dist.barrier()
     finally:
+        # Every wait a rank can meet is bounded (the device-side waits at 2 s, the process group at 60 s), so
+        # a rank that fails gets here by itself and releases its outputs (and their multicast binding) before
+        # it exits; nothing ends it from outside.
+        torch.cuda.synchronize()
+        if fused is not None:
+            fused.close()
+        if full is not None:
+            full.close()
+        if ctx is not None:
+            ctx.close()
         dist.destroy_process_group()
 
 
@@ -70,10 +79,10 @@ def test_fused_gather_matches_single_gpu_product(multicast):
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=240)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
+        p.join(timeout=600)
+    # A rank still alive here has outlived every bound it waits under; the test fails without ending it
+    # from outside (its outputs may be bound to an NVLink multicast object).
+    assert not any(p.is_alive() for p in procs), "a rank did not exit within its bounded waits"
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     got = dict(results)
     assert got[0] is True and got[1] is True, got

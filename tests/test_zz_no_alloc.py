@@ -1,7 +1,10 @@
 """sc_linear_ex_noalloc (scratch in a static device array of the library) against sc_linear_ex (the
-caller's workspace), through the C ABI on a B200: the same outputs within the bars of
-test_gpu_linear.py (fp32: relative L2 <= 1e-5; bf16: relative L2 <= 1e-3 and max-abs <= 2e-2), on
-two calls in a row that share the array, and a clear refusal above the array's 32 MiB."""
+caller's workspace), through the C ABI on a B200.  Both run the same kernels on the same operands, so
+their outputs must agree bit for bit; the check alternates different weights (A, B, A, one of them a
+convrot weight whose rotated x sits in front of the widened copy inside the array) so that a stale
+widened tile or rotated row left by the previous call would show, and ends with a clear refusal above
+the array's 32 MiB.  Callers of this entry point are bindings that have no scratch buffer to pass and
+may not allocate per call."""
 import ctypes
 
 import numpy as np
@@ -16,9 +19,6 @@ if not torch.cuda.is_available():  # collected on CPU boxes, skipped there
     pytest.skip("needs a CUDA device", allow_module_level=True)
 
 from siliconed_b200.products import Context, QuantizedWeight  # noqa: E402
-
-REL_L2_BF16, MAX_ABS_BF16, REL_L2_F32 = 1e-3, 2e-2, 1e-5
-
 
 @pytest.fixture(scope="module")
 def ctx():
@@ -49,20 +49,12 @@ def noalloc(ctx, w, x, m, b, f32):
     return out
 
 
-def as_f64(t):
-    if t.dtype == torch.bfloat16:
-        t = t.float()
-    return t.cpu().numpy().astype(np.float64)
+def bits(t):
+    return t.view(torch.int32 if t.dtype == torch.float32 else torch.int16)
 
 
-def rel_l2(a, b):
-    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
-
-
-@pytest.mark.parametrize("kind,m,k,n", [(abi.WEIGHT_INT8, 2048, 3072, 3072), (abi.WEIGHT_E4M3, 1600, 2048, 1000)])
-def test_noalloc_matches_the_workspace_entry_point(ctx, kind, m, k, n):
-    g = np.random.default_rng(m + k + n)
-    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+def make_weight(ctx, kind, k, n, seed, rotation=0):
+    g = np.random.default_rng(seed)
     if kind == abi.WEIGHT_INT8:
         q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
         s = (np.abs(g.standard_normal(n)) * 0.02 / 127 + 1e-7).astype(np.float32)
@@ -71,22 +63,39 @@ def test_noalloc_matches_the_workspace_entry_point(ctx, kind, m, k, n):
         q[(q & 0x7F) == 0x7F] ^= 1
         s = (np.abs(g.standard_normal(n)) * 0.02 / 448 + 1e-7).astype(np.float32)
     b = configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.01)
-    w = QuantizedWeight(ctx, q, kind, s)
-    assert 0 < w.workspace_bytes(m) <= 32 << 20      # the widened route, inside the static scratch
-    xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.bfloat16)
+    w = QuantizedWeight(ctx, q, kind, s, rotation=rotation)
     bd = torch.from_numpy(b.view(np.int16)).cuda().view(torch.bfloat16)
+    return w, bd
+
+
+def test_noalloc_matches_the_workspace_entry_point_bit_for_bit(ctx):
+    # A: config 1's shape (its tiles take the widening inside the GEMM); B: e4m3 (widen, then the GEMM);
+    # R: convrot (the rotated x, then the widened copy, both in the array)
+    weights = {
+        "A": make_weight(ctx, abi.WEIGHT_INT8, 3072, 3072, 1) + (4096,),
+        "B": make_weight(ctx, abi.WEIGHT_E4M3, 2048, 1000, 2) + (2048,),
+        "R": make_weight(ctx, abi.WEIGHT_INT8, 3072, 2560, 3, rotation=64) + (2048,),
+    }
+    g = np.random.default_rng(4)
+    xs = {}
+    for name, (w, _, m) in weights.items():
+        need = w.workspace_bytes(m)
+        assert 0 < need <= 32 << 20, (name, need)       # the widened route, inside the static scratch
+        x = configs.to_bf16_bits(g.standard_normal((m, w.k), dtype=np.float32))
+        xs[name] = torch.from_numpy(x.view(np.int16)).cuda().view(torch.bfloat16)
+    refs = {}
+    for name, (w, bd, m) in weights.items():
+        for f32 in (True, False):
+            refs[name, f32] = existing(ctx, w, xs[name], m, bd, f32)
+    order = ["A", "B", "A", "R", "B", "R", "A"]         # consecutive calls share the array
     for f32 in (True, False):
-        ref = as_f64(existing(ctx, w, xd, m, bd, f32))
-        for call in range(2):                         # two calls in a row share the array
-            got = as_f64(noalloc(ctx, w, xd, m, bd, f32))
+        for call, name in enumerate(order):
+            w, bd, m = weights[name]
+            got = noalloc(ctx, w, xs[name], m, bd, f32)
             ctx.poll_errors()
-            e = rel_l2(got, ref)
-            if f32:
-                assert e <= REL_L2_F32, (call, e)
-            else:
-                mx = float(np.max(np.abs(got - ref)))
-                assert e <= REL_L2_BF16 and mx <= MAX_ABS_BF16, (call, e, mx)
-    w.close()
+            assert torch.equal(bits(got), bits(refs[name, f32])), (f32, call, name)
+    for w, _, _ in weights.values():
+        w.close()
 
 
 def test_noalloc_refuses_scratch_beyond_its_array(ctx):
