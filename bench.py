@@ -388,6 +388,102 @@ def run_ours(args):
     return 0
 
 
+CHAIN_LAYERS = 8
+
+
+def run_chain(args):
+    """chainM (M = 1, 4, 16, 32): the decode case of config 4 as a model runs it, eight distinct int8 weights
+    back to back, [12288 out, 4096 in] and [4096 out, 12288 in] alternating (an MLP's up and down products),
+    each layer's bf16 output the next one's input; every weight is read cold (400 MB in all, beyond the L2),
+    the L2 flushed once before each chain.  A step is one pass through the eight layers; value: the chain's
+    algorithmic bytes (every weight, scale, input and output once) over its time, per second."""
+    import torch
+    from siliconed_b200 import configs
+    from siliconed_b200.products import Context, QuantizedWeight
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(local)
+    m = int(args.workload[5:])
+    ctx = Context(local)
+    shapes = [(12288, 4096), (4096, 12288)] * (CHAIN_LAYERS // 2)
+    cases = [configs.config4(m, n, k, seed=i) for i, (n, k) in enumerate(shapes)]
+    weights = [QuantizedWeight(ctx, c.codes_nk, c.kind, c.scales, published_nk=True) for c in cases]
+    acts = [torch.from_numpy(cases[0].x.view(np.int16)).cuda().view(torch.bfloat16)]
+    for n, _ in shapes:
+        acts.append(torch.empty((m, n), dtype=torch.bfloat16, device="cuda"))
+    ws = torch.empty(max(max(w.workspace_bytes(m) for w in weights), 1), dtype=torch.uint8, device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    clean = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    chain_bytes = sum(c.bytes_moved() for c in cases)
+
+    def step():
+        for i, w in enumerate(weights):
+            w.linear(acts[i], out=acts[i + 1], workspace=ws, stream=stream)
+
+    for _ in range(args.warmup):
+        flush.fill_(1)
+        torch.sum(clean, dim=0, out=sink)
+        step()
+    ctx.poll_errors()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        torch.cuda._sleep(int(2e6) * max(1, args.steps // 5))
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            torch.sum(clean, dim=0, out=sink)
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    ctx.poll_errors()
+    per = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    ms = sum(per) / len(per)
+    value = chain_bytes / (ms / 1e3) / 1e9
+    # the first two layers one at a time, each after its own flush (the single cold read)
+    single = []
+    for i, w in enumerate(weights[:2]):
+        ev = []
+        for r in range(max(args.steps, 3)):
+            flush.fill_(r & 0xFF)
+            torch.sum(clean, dim=0, out=sink)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            w.linear(acts[i], out=acts[i + 1], workspace=ws, stream=stream)
+            b.record(stream)
+            ev.append((a, b))
+        torch.cuda.synchronize()
+        t = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+        single.append({"shape": list(shapes[i]), "us": t * 1e3, "gb_s": cases[i].bytes_moved() / (t / 1e3) / 1e9})
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        kern = "gemv_w8" if m <= 4 else "gemm_w8_skinny"
+        line = {"metric": "int8-weight GEMV achieved HBM GB/s (decode chain, per layer)", "value": value,
+                "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic",
+                "config": {"workload": f"{args.workload}: {CHAIN_LAYERS} distinct int8 per-channel weights, "
+                                       f"[12288, 4096] and [4096, 12288] alternating, x bf16 [{m}, K], each "
+                                       f"output the next input", "m": m, "layers": CHAIN_LAYERS,
+                           "bytes_per_chain": chain_bytes,
+                           "l2": "flushed once before each chain (400 MB of weights, beyond the L2)",
+                           "parallelism": "one GPU"},
+                "roofline": {"bound": "hbm", "achieved": value, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                             "frac": value / peaks["hbm_gbs"], "traffic": None, "peak_source": peak_src,
+                             "kernels": [kern]},
+                "single_cold_read": single, "clocks": clocks.summary(), "gpu_launches": args.steps * CHAIN_LAYERS,
+                "step_ms_min": min(per), "step_ms_median": statistics.median(per)}
+        print(json.dumps(line), flush=True)
+    for w in weights:
+        w.close()
+    ctx.close()
+    return 0
+
+
 def run_scale(args):
     """Config 1 on N > 1 GPUs, the default workload there (strong scaling: the total work is config 1's one
     product whatever N is).  Rank r registers W's columns column_ranges(N, P)[r] and multiplies the whole x
@@ -892,6 +988,8 @@ def main():
         return run_colpar(args)
     if args.workload == "cfg1" and args.impl == "ours" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
         return run_scale(args)
+    if args.workload.startswith("chain") and args.impl == "ours":
+        return run_chain(args)
     if args.workload in DIT_WORKLOADS:
         if args.impl == "reference":
             rank = int(os.environ.get("RANK", "0"))

@@ -9,7 +9,9 @@
 // shared memory and are added in slice order, so every run gives the same bits; nothing is kept
 // outside the CTA (no global scratch, no cross-CTA synchronisation), which is what the reference's
 // split GEMV achieves with its fixed-order sum of partials (Sources/Siliconed/DecodeKernels.swift:20-23,
-// :67-109).
+// :67-109).  Launched with programmatic dependent launch: a CTA starts its weight bytes (an L2 prefetch of
+// its rows and its first batch of loads) before it waits for the kernel ahead of it, whose output is x in a
+// decode step, so consecutive products' weight reads overlap.
 #include <cuda_bf16.h>
 
 #include "sc_codes.cuh"
@@ -106,6 +108,13 @@ __global__ void __launch_bounds__(kThreads) gemv_w8(const uint8_t* __restrict__ 
   const int row0 = blockIdx.x * RB + rg * RW;
   const uint8_t* wrow = values + static_cast<int64_t>(row0) * k_pad;
 
+  // In a decode step the products run back to back and x is the previous product's output, while the
+  // weight bytes depend on nothing: the next kernel of the stream may launch now, this CTA's rows (RB
+  // contiguous rows of the arena) start toward the L2, and its first batch of loads is issued before the
+  // wait for the previous kernel (for config 4's shapes the first batch is a warp's whole share).
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) prefetch_l2_bulk(values + static_cast<int64_t>(blockIdx.x) * RB * k_pad, RB * k_pad);
+  bool waited = false;
   unsigned long long acc[RW][MT];
 #pragma unroll
   for (int r = 0; r < RW; ++r)
@@ -120,6 +129,10 @@ __global__ void __launch_bounds__(kThreads) gemv_w8(const uint8_t* __restrict__ 
 #pragma unroll
       for (int r = 0; r < RW; ++r)
         wv[u][r] = kb < kend ? ld_stream(wrow + static_cast<int64_t>(r) * k_pad + kb) : make_uint4(0, 0, 0, 0);
+    }
+    if (!waited) {  // the first batch of weight bytes is in flight before the wait for the previous kernel
+      pdl_wait();
+      waited = true;
     }
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
@@ -150,6 +163,7 @@ __global__ void __launch_bounds__(kThreads) gemv_w8(const uint8_t* __restrict__ 
     }
   }
 
+  if (!waited) pdl_wait();
   // Pairs, then lanes (fixed butterfly), then this warp's K slice to shared memory.
 #pragma unroll
   for (int r = 0; r < RW; ++r)
@@ -183,10 +197,18 @@ cudaError_t launch_ks(const sc_weight* w, const uint16_t* x, int64_t m, const ui
                       cudaStream_t stream) {
   constexpr int RB = (kWarps / KS) * RW;
   const unsigned grid = static_cast<unsigned>(w->n_pad / RB);
-  gemv_w8<kKind, kNaN, MT, KS, kF32Out><<<grid, kThreads, 0, stream>>>(
-      w->values, static_cast<int>(w->k_pad), w->scales, x, static_cast<int>(m), static_cast<int>(w->k), bias, y,
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_w8<kKind, kNaN, MT, KS, kF32Out>, static_cast<const uint8_t*>(w->values),
+      static_cast<int>(w->k_pad), static_cast<const float*>(w->scales), x, static_cast<int>(m), static_cast<int>(w->k), bias, y,
       static_cast<int>(w->n), m0);
-  return cudaGetLastError();
 }
 
 template <int kKind, bool kNaN, int MT, bool kF32Out>
