@@ -77,6 +77,14 @@ typedef enum sc_in_type { SC_IN_BF16 = 0, SC_IN_F32 = 1 } sc_in_type;
 /* Flags of sc_weight_create. */
 #define SC_WEIGHT_VALUES_ON_DEVICE 0x1u /* values and scales are device pointers (else host) */
 #define SC_WEIGHT_PUBLISHED_NK 0x2u     /* values are the published [N, K] rows, not the map's [K, N] */
+/* values are already in the arena's own layout (a map stored re-tiled, `"layout": "arena"`): the rows
+ * [n_pad][k_pad] bytes of the transposed weight, n_pad = N rounded up to 256, k_pad = K rounded up to 64,
+ * int8 stored biased (q + 128), e4m3 as published, every padding byte the code of zero.  Registration is
+ * then one copy, no re-tiling kernel; the whole weight only (not with SC_WEIGHT_PUBLISHED_NK, no shard).
+ * Host values are checked (padding, NaN codes); device values are trusted, and SC_WEIGHT_NAN_CODES states
+ * that an e4m3 weight holds NaN codes (0x7F / 0xFF). */
+#define SC_WEIGHT_ARENA_LAYOUT 0x4u
+#define SC_WEIGHT_NAN_CODES 0x8u
 
 typedef uint16_t sc_bf16;
 typedef struct sc_ctx sc_ctx;

@@ -24,7 +24,7 @@ STATUS_NAMES = {0: "SC_OK", 1: "SC_INVALID_ARG", 2: "SC_UNSUPPORTED_SHAPE", 3: "
 WEIGHT_INT8, WEIGHT_E4M3 = 1, 2
 SCALE_F32, SCALE_BF16, SCALE_F16 = 1, 2, 3
 SCALE_TENSOR, SCALE_COLUMNS = 0, 1
-VALUES_ON_DEVICE, PUBLISHED_NK = 0x1, 0x2
+VALUES_ON_DEVICE, PUBLISHED_NK, ARENA_LAYOUT, NAN_CODES = 0x1, 0x2, 0x4, 0x8
 OUT_BF16, OUT_F32 = 0, 1
 EPI_GELU_TANH, EPI_GATED_RESIDUAL, EPI_SWIGLU = 1, 2, 3
 IN_BF16, IN_F32 = 0, 1

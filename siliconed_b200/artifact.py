@@ -26,6 +26,15 @@ boundary after its values; and ``forge_linear`` restates the forge's move of a p
 weight ``[N, K]`` with its per-row scale ``[N, 1]`` (or one for the tensor) to the map's ``[K, N]`` with
 a scale ``[N]`` (QuantizedMapTests.swift:149-216: the published bytes transposed, the scales as
 published, in their own type).
+
+This library extends the map with one tensor key, ``"layout": "arena"`` (``forge_linear(...,
+layout="arena")``): an 8-bit linear whose codes are stored as the device arena keeps them, rows of K for
+each output, ``[n_pad][k_pad]`` with N padded to 256 and K to 64, int8 biased by 128, every padding byte
+the code of zero (``"nan_codes": true`` when an e4m3 tensor holds NaN codes); its scale follows at the next
+16-byte boundary as published.  Registering such a tensor is one copy into the arena, with no staging
+buffer and no re-tiling kernel (SC_WEIGHT_ARENA_LAYOUT); ``values`` still returns the published
+``[K, N]`` codes (a decoded copy) and ``stored`` the bytes as they lie.  Maps without the key are read as
+the reference writes them.
 """
 from __future__ import annotations
 
@@ -54,6 +63,7 @@ PACKED_BLOCKS = {"q4_0": (32, 18), "q4_1": (32, 20), "q5_0": (32, 22), "q5_1": (
 SQ_BITS = {"sq4": 4, "sq5": 5}
 SQ_GROUP, SQ_ROTATION = 16, 256
 SCALE_TYPES = ("bfloat16", "float16", "float32")
+ARENA_N, ARENA_K = 256, 64  # the library's arena tiles: N padded to 256 rows, K to 64 bytes
 DTYPES = tuple(VALUE_SIZES) + tuple(PACKED_BLOCKS) + tuple(SQ_BITS)
 
 
@@ -146,6 +156,8 @@ class Tensor:
     dtype: str
     scale: Scale | None = None
     rotation: Rotation | None = None
+    layout: str | None = None   # "arena": the codes stored re-tiled, [n_pad][k_pad] (this library's extension)
+    nan_codes: bool = False     # an arena-layout e4m3 tensor holding NaN codes (0x7F / 0xFF)
 
     @property
     def count(self) -> int:
@@ -154,6 +166,23 @@ class Tensor:
     @property
     def is_quantized(self) -> bool:
         return self.dtype in ("int8", "float8_e4m3")
+
+
+def arena_dims(k: int, n: int) -> tuple[int, int]:
+    """(n_pad, k_pad) of a [K, N] weight in the library's arena: N rounded up to 256, K to 64."""
+    return -(-n // ARENA_N) * ARENA_N, -(-k // ARENA_K) * ARENA_K
+
+
+def arena_codes(values_nk: np.ndarray, dtype: str) -> np.ndarray:
+    """The arena's bytes [n_pad][k_pad] of published codes [N, K]: rows of K contiguous, int8 stored biased
+    (q + 128), e4m3 as published, every padding byte the code of zero (0x80 for int8, 0x00 for e4m3)."""
+    q = np.ascontiguousarray(values_nk).view(np.uint8)
+    n, k = q.shape
+    n_pad, k_pad = arena_dims(k, n)
+    zero = 0x80 if dtype == "int8" else 0x00
+    out = np.full((n_pad, k_pad), zero, np.uint8)
+    out[:n, :k] = (q ^ 0x80) if dtype == "int8" else q
+    return out
 
 
 def _scale_entry(raw, name: str, shape: list[int], dtype: str) -> Scale:
@@ -247,6 +276,17 @@ def parse(buf, size: int) -> tuple[dict, int, list[str], dict[str, Tensor]]:
         if count is None:
             raise MapError("bad_header", f"{name}: shape {shape}")
         scale = _scale_entry(entry["scale"], name, shape, dtype) if "scale" in entry else None
+        layout = entry.get("layout")
+        if layout is not None:
+            # this library's extension: an 8-bit linear stored as its arena keeps it (values [n_pad][k_pad])
+            if layout != "arena" or dtype not in ("int8", "float8_e4m3") or len(shape) != 2 or \
+                    (scale is not None and scale.block is not None) or not isinstance(entry.get("nan_codes", False), bool):
+                raise MapError("bad_header", f"{name}: layout {layout!r} on {dtype} {shape}")
+            n_pad, k_pad = arena_dims(shape[0], shape[1])
+            stored = n_pad * k_pad
+            if scale is not None and scale.offset < stored:
+                raise MapError("bad_header", f"{name}: a scale at {scale.offset} inside the {stored} arena bytes")
+            count = stored if scale is None else count
         if dtype in PACKED_BLOCKS:
             values, per = PACKED_BLOCKS[dtype]
             if len(shape) != 2 or shape[0] % values != 0 or "scale" in entry or "rotation" in entry:
@@ -268,7 +308,8 @@ def parse(buf, size: int) -> tuple[dict, int, list[str], dict[str, Tensor]]:
         if expected > INT_MAX or nbytes != expected:
             raise MapError("bad_header", f"{name}: {nbytes} bytes for {shape} of {dtype}")
         rotation = _rotation_entry(entry["rotation"], name, shape, dtype, scale) if "rotation" in entry else None
-        tensors[name] = Tensor(name, offset, nbytes, tuple(shape), dtype, scale, rotation)
+        tensors[name] = Tensor(name, offset, nbytes, tuple(shape), dtype, scale, rotation, layout,
+                               bool(entry.get("nan_codes", False)))
     if set(order) != set(tensors):
         raise MapError("bad_header", "`order` and `tensors` disagree")
     return header, page, list(order), tensors
@@ -362,11 +403,23 @@ class Artifact:
         return np.frombuffer(self._mm, dtype=np.uint8, count=t.bytes, offset=t.offset)
 
     def values(self, name: str) -> np.ndarray:
-        """An 8-bit tensor's codes in the map's layout (``[K, N]`` for a linear), uint8, zero-copy."""
+        """An 8-bit tensor's codes in the map's layout (``[K, N]`` for a linear), uint8, zero-copy; for a
+        tensor stored in the arena layout, a copy decoded back to ``[K, N]`` as published."""
         t = self.tensor(name)
         if not t.is_quantized:
             raise MapError("bad_header", f"{name}: {t.dtype} is not an 8-bit type", self.path)
+        if t.layout == "arena":
+            a = self.stored(name)[: t.shape[1], : t.shape[0]]
+            return np.ascontiguousarray((a ^ 0x80) if t.dtype == "int8" else a).T.copy()
         return np.frombuffer(self._mm, dtype=np.uint8, count=t.count, offset=t.offset).reshape(t.shape)
+
+    def stored(self, name: str) -> np.ndarray:
+        """An arena-layout tensor's bytes as stored, ``[n_pad, k_pad]``, zero-copy."""
+        t = self.tensor(name)
+        if t.layout != "arena":
+            raise MapError("bad_header", f"{name}: not stored in the arena layout", self.path)
+        n_pad, k_pad = arena_dims(t.shape[0], t.shape[1])
+        return np.frombuffer(self._mm, dtype=np.uint8, count=n_pad * k_pad, offset=t.offset).reshape(n_pad, k_pad)
 
     def scale_values(self, name: str) -> tuple[str, np.ndarray] | None:
         """(dtype, scale) of an 8-bit tensor, zero-copy: float32 / float16 arrays, bf16 as uint16 bits;
@@ -450,6 +503,9 @@ class Artifact:
             if st == "bfloat16":
                 scale_type = abi.SCALE_BF16
         rotation = t.rotation.group if t.rotation is not None else 0
+        if t.layout == "arena":  # one copy into the device arena, no re-tiling
+            return QuantizedWeight(ctx, self.stored(name), kind, scales, scale_type=scale_type, rotation=rotation,
+                                   arena=t.shape, nan_codes=t.nan_codes, **kw)
         return QuantizedWeight(ctx, self.values(name), kind, scales, scale_type=scale_type, rotation=rotation, **kw)
 
     def quantized_names(self) -> list[str]:
@@ -475,9 +531,14 @@ class MapTensor:
     block: int | None = None
     rotation: int | None = None
     transposed: bool | None = None
+    layout: str | None = None      # "arena": data holds the arena bytes [n_pad][k_pad] (arena_codes)
+    nan_codes: bool | None = None
 
     def value_bytes(self) -> int:
         count = element_count(self.shape)
+        if self.layout == "arena":
+            n_pad, k_pad = arena_dims(self.shape[0], self.shape[1])
+            return n_pad * k_pad
         if self.dtype in SQ_BITS:
             return self.shape[1] * sq_row_bytes(self.shape[0], SQ_BITS[self.dtype])
         if self.dtype in PACKED_BLOCKS:
@@ -524,6 +585,10 @@ def write_map(path: str, tensors: list[MapTensor], header: dict | None = None, p
                 e["scale"] = s
             if t.rotation:
                 e["rotation"] = {"kind": "convrot", "group": int(t.rotation)}
+            if t.layout is not None:
+                e["layout"] = t.layout
+                if t.nan_codes:
+                    e["nan_codes"] = True
             table[t.name] = e
         h = {"format": 1, "page": page, "linear_weights_transposed": True}
         h.update(header or {})
@@ -567,7 +632,7 @@ def _scale_as_f32(s: np.ndarray, scale_dtype: str) -> np.ndarray:
 
 
 def forge_linear(name: str, values_nk: np.ndarray, scales: np.ndarray | None, dtype: str, scale_dtype: str | None,
-                 rotation: int | None = None) -> MapTensor:
+                 rotation: int | None = None, layout: str | None = None) -> MapTensor:
     """A published 8-bit ``nn.Linear`` weight as the map keeps it (the forge's ``kept8bit`` outcome,
     QuantizedMapTests.swift:149-216): the codes ``[N, K]`` transposed to ``[K, N]`` byte for byte, the
     scale (``[N, 1]`` / ``[N]`` per output row, or ``[]`` / ``[1]`` for the tensor) kept in its published
@@ -576,7 +641,11 @@ def forge_linear(name: str, values_nk: np.ndarray, scales: np.ndarray | None, dt
     Refused (``ForgeRefusal``), as the forge does: an int8 weight without a scale (an fp8 one without a
     scale is a plain cast, w = f8); a scale shaped otherwise than one per tensor or one per row; a nonzero
     scale whose smallest product ``|s| * min|q| / sqrt(G)`` is subnormal in fp32 (min|q| = 1 for int8,
-    2^-9 for e4m3; ``QuantizedLayouts.checkSubnormal``, Forge/Quantization.swift:380-402)."""
+    2^-9 for e4m3; ``QuantizedLayouts.checkSubnormal``, Forge/Quantization.swift:380-402).
+
+    ``layout="arena"`` (this library's extension of the map) stores the codes as the device arena keeps
+    them (``arena_codes``: [n_pad][k_pad], int8 biased), so that registering the tensor is one copy with
+    no re-tiling kernel; the header records ``"layout": "arena"`` and, for e4m3, whether NaN codes occur."""
     if dtype not in ("int8", "float8_e4m3"):
         raise ForgeRefusal(f"{name}: {dtype} is not an 8-bit weight type")
     q = np.ascontiguousarray(values_nk).view(np.uint8)
@@ -607,5 +676,11 @@ def forge_linear(name: str, values_nk: np.ndarray, scales: np.ndarray | None, dt
         raise ForgeRefusal(f"{name}: a scale whose products can fall below 2^-126 (subnormal)")
     if rotation and (dtype != "int8" or not is_rotation_group(rotation) or k % rotation != 0):
         raise ForgeRefusal(f"{name}: rotation convrot of group {rotation} on {dtype} [{n}, {k}]")
+    if layout == "arena":
+        nan = dtype == "float8_e4m3" and bool(np.any((q & 0x7F) == 0x7F))
+        return MapTensor(name, dtype, (k, n), arena_codes(q, dtype), s.reshape(s_shape), scale_dtype, s_shape,
+                         rotation=rotation, transposed=True, layout="arena", nan_codes=nan)
+    if layout is not None:
+        raise ForgeRefusal(f"{name}: unknown layout {layout!r}")
     return MapTensor(name, dtype, (k, n), np.ascontiguousarray(q.T), s.reshape(s_shape), scale_dtype, s_shape,
                      rotation=rotation, transposed=True)

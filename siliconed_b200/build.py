@@ -22,7 +22,7 @@ DIT_LIB = os.path.join(HERE, "libsiliconed_dit.so")
 DIT_CSRC = os.path.join(CSRC, "dit")
 DIT_SOURCES = ["sd_kernels.cu"]
 
-SOURCES = ["sc_abi.cu", "sc_weight.cu", "sc_gemm.cu", "sc_gemm_pair.cu", "sc_gemm_bf16.cu", "sc_gemm_skinny.cu",
+SOURCES = ["sc_abi.cu", "sc_weight.cu", "sc_gemm.cu", "sc_gemm_pair.cu", "sc_gemm_bf16.cu", "sc_gemm_skinny.cu", "sc_gemm_skinny_sk.cu",
            "sc_gemv.cu", "sc_no_alloc.cu", "sc_rotate.cu", "sc_w8a8.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

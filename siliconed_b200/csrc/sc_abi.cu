@@ -204,17 +204,18 @@ sc_status rotate_operand(sc_ctx* ctx, const sc_weight* w, const sc_bf16*& x, int
   return SC_OK;
 }
 
-// Whether a product on stream `st` may run the widening inside its GEMM, which uses the context's one set of
-// readiness counters: yes unless the last launch that used them went to another stream and may still be
-// running (then the product takes the separate widening, which gives the same bits and shares nothing).
-// Under stream capture nothing can be asked of an event, and the separate widening is taken.
-sc_status fused_widen_free(sc_ctx* ctx, cudaStream_t st, bool& free) {
+// Whether a product on stream `st` may use a set of the context's counters (the fused widening's readiness
+// counters, the streamed skinny product's tile counters): yes unless the last launch that used them went to
+// another stream and may still be running (then the product takes a route without them, which gives the
+// same bits and shares nothing).  Under stream capture nothing can be asked of an event, and the route
+// without them is taken.
+sc_status counters_free(sc_ctx* ctx, const sc_counter_guard& g, cudaStream_t st, bool& free) {
   free = false;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaError_t e = cudaStreamIsCapturing(st, &cap); e != cudaSuccess) return check_cuda(ctx, e, "capture query");
   if (cap != cudaStreamCaptureStatusNone) return SC_OK;
-  if (ctx->fw_launched && ctx->fw_stream != st) {
-    const cudaError_t e = cudaEventQuery(ctx->fw_event);
+  if (g.launched && g.stream != st) {
+    const cudaError_t e = cudaEventQuery(g.event);
     if (e == cudaErrorNotReady) {
       cudaGetLastError();
       return SC_OK;
@@ -225,16 +226,16 @@ sc_status fused_widen_free(sc_ctx* ctx, cudaStream_t st, bool& free) {
   return SC_OK;
 }
 
-// Records the stream and completion event of a launch that used the readiness counters.
-sc_status fused_widen_launched(sc_ctx* ctx, cudaStream_t st) {
-  if (ctx->fw_event == nullptr) {
-    sc_status s = check_cuda(ctx, cudaEventCreateWithFlags(&ctx->fw_event, cudaEventDisableTiming), "event");
+// Records the stream and completion event of a launch that used a set of counters.
+sc_status counters_launched(sc_ctx* ctx, sc_counter_guard& g, cudaStream_t st) {
+  if (g.event == nullptr) {
+    sc_status s = check_cuda(ctx, cudaEventCreateWithFlags(&g.event, cudaEventDisableTiming), "event");
     if (s != SC_OK) return s;
   }
-  sc_status s = check_cuda(ctx, cudaEventRecord(ctx->fw_event, st), "event record");
+  sc_status s = check_cuda(ctx, cudaEventRecord(g.event, st), "event record");
   if (s != SC_OK) return s;
-  ctx->fw_stream = st;
-  ctx->fw_launched = true;
+  g.stream = st;
+  g.launched = true;
   return SC_OK;
 }
 
@@ -262,6 +263,21 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
   CUtensorMap tmx;
   if (m <= 32) {
     if ((s = make_tmap_x(ctx, x, m, w->k, &tmx, gemm_skinny_box_rows(m))) != SC_OK) return s;
+    // With the workspace for the tiles' partials: every SM streams an equal share of the weight.  Without
+    // it: the cluster kernel, whose K parts meet in distributed shared memory.
+    const int grid = skinny_sk_grid(w, ctx->sm_count);
+    bool streamed = false;
+    if (grid > 0 && workspace != nullptr && workspace_bytes >= skinny_sk_workspace_bytes(grid) &&
+        (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0 &&
+        (s = counters_free(ctx, ctx->skinny_guard, st, streamed)) != SC_OK)
+      return s;
+    if (streamed) {
+      if ((s = check_cuda(ctx, launch_gemm_skinny_sk(tmx, w, bias, y, f32_out, m, static_cast<float*>(workspace),
+                                                     ctx->d_skinny, grid, ctx->d_err, st),
+                          "streamed skinny gemm launch")) != SC_OK)
+        return s;
+      return counters_launched(ctx, ctx->skinny_guard, st);
+    }
     return check_cuda(ctx, launch_gemm_skinny(tmx, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
                       "skinny gemm launch");
   }
@@ -275,7 +291,7 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
       CUtensorMap tmw;
       if ((s = make_tmap_widened(ctx, w, workspace, &tmw)) != SC_OK) return s;
       bool fused = false;
-      if (fused_widen_fits(w, m, ctx->sm_count) && (s = fused_widen_free(ctx, st, fused)) != SC_OK) return s;
+      if (fused_widen_fits(w, m, ctx->sm_count) && (s = counters_free(ctx, ctx->widen_guard, st, fused)) != SC_OK) return s;
       if (fused) {
         // a few rounds of tiles: the GEMM's CTAs widen the codes themselves, the first round's columns
         // first, the rest while the pipeline runs
@@ -283,7 +299,7 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
                                                      ctx->d_err, ctx->sm_count, st),
                             "bf16 pair gemm (fused widening) launch")) != SC_OK)
           return s;
-        return fused_widen_launched(ctx, st);
+        return counters_launched(ctx, ctx->widen_guard, st);
       }
       if ((s = check_cuda(ctx, launch_widen(w, workspace, ctx->sm_count, st), "widen launch")) != SC_OK) return s;
       return check_cuda(ctx, launch_gemm_bf16(tmx, tmw, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
@@ -354,10 +370,13 @@ sc_status sc_ctx_create(int device, sc_ctx** out) {
   if (cudaMalloc(&ctx->d_err, kCtxWords * sizeof(int)) != cudaSuccess ||
       cudaMemset(ctx->d_err, 0, kCtxWords * sizeof(int)) != cudaSuccess ||
       cudaMalloc(&ctx->d_widen, (kWidenCounterWords + 32) * sizeof(uint32_t)) != cudaSuccess ||
-      cudaMemset(ctx->d_widen, 0, (kWidenCounterWords + 32) * sizeof(uint32_t)) != cudaSuccess) {
+      cudaMemset(ctx->d_widen, 0, (kWidenCounterWords + 32) * sizeof(uint32_t)) != cudaSuccess ||
+      cudaMalloc(&ctx->d_skinny, kSkinnyCounterWords * sizeof(uint32_t)) != cudaSuccess ||
+      cudaMemset(ctx->d_skinny, 0, kSkinnyCounterWords * sizeof(uint32_t)) != cudaSuccess) {
     cudaGetLastError();
     if (ctx->d_err) cudaFree(ctx->d_err);
     if (ctx->d_widen) cudaFree(ctx->d_widen);
+    if (ctx->d_skinny) cudaFree(ctx->d_skinny);
     delete ctx;
     return SC_OUT_OF_MEMORY;
   }
@@ -372,7 +391,9 @@ void sc_ctx_destroy(sc_ctx* ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->d_widen) cudaFree(ctx->d_widen);
-  if (ctx->fw_event) cudaEventDestroy(ctx->fw_event);
+  if (ctx->d_skinny) cudaFree(ctx->d_skinny);
+  if (ctx->widen_guard.event) cudaEventDestroy(ctx->widen_guard.event);
+  if (ctx->skinny_guard.event) cudaEventDestroy(ctx->skinny_guard.event);
   for (cudaEvent_t e : ctx->host_events)
     if (e) cudaEventDestroy(e);
   if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
@@ -393,9 +414,15 @@ sc_status sc_weight_create_shard(sc_ctx* ctx, const void* values, sc_weight_kind
   if (scale_type != SC_SCALE_F32 && scale_type != SC_SCALE_BF16 && scale_type != SC_SCALE_F16)
     return fail(ctx, SC_INVALID_ARG, "unknown scale type");
   if (layout != SC_SCALE_TENSOR && layout != SC_SCALE_COLUMNS) return fail(ctx, SC_INVALID_ARG, "unknown scale layout");
-  if (flags & ~(SC_WEIGHT_VALUES_ON_DEVICE | SC_WEIGHT_PUBLISHED_NK)) return fail(ctx, SC_INVALID_ARG, "unknown flags");
+  if (flags & ~(SC_WEIGHT_VALUES_ON_DEVICE | SC_WEIGHT_PUBLISHED_NK | SC_WEIGHT_ARENA_LAYOUT | SC_WEIGHT_NAN_CODES))
+    return fail(ctx, SC_INVALID_ARG, "unknown flags");
   if (k <= 0 || n <= 0) return fail(ctx, SC_INVALID_ARG, "k and n must be positive");
   if (n_begin < 0 || n_end > n || n_begin >= n_end) return fail(ctx, SC_INVALID_ARG, "bad column range");
+  const bool arena_layout = (flags & SC_WEIGHT_ARENA_LAYOUT) != 0;
+  if (arena_layout && ((flags & SC_WEIGHT_PUBLISHED_NK) || n_begin != 0 || n_end != n))
+    return fail(ctx, SC_INVALID_ARG, "the arena layout is the whole weight's, not a published [N, K] nor a shard");
+  if ((flags & SC_WEIGHT_NAN_CODES) && !arena_layout)
+    return fail(ctx, SC_INVALID_ARG, "SC_WEIGHT_NAN_CODES goes with SC_WEIGHT_ARENA_LAYOUT");
   sc_status s = enter(ctx);
   if (s != SC_OK) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -446,6 +473,42 @@ sc_status sc_weight_create_shard(sc_ctx* ctx, const void* values, sc_weight_kind
     delete w;
     return st_;
   };
+  if (arena_layout) {
+    // The codes already lie as the arena keeps them: on the host they are checked here (K and N padding
+    // the code of zero, so that no padded product can be a NaN; NaN codes of e4m3 found), then copied once.
+    const uint8_t* v = static_cast<const uint8_t*>(values);
+    const uint8_t zero = kind == SC_WEIGHT_INT8 ? kPadInt8 : kPadE4M3;
+    bool nan_codes = (flags & SC_WEIGHT_NAN_CODES) != 0;
+    if (!on_device) {
+      nan_codes = false;
+      for (int64_t r = 0; r < w->n_pad; ++r) {
+        const uint8_t* row = v + r * w->k_pad;
+        for (int64_t c = (r < cols ? k : 0); c < w->k_pad; ++c)
+          if (row[c] != zero) {
+            delete w;
+            return fail(ctx, SC_INVALID_ARG, "arena layout: a padding code that is not the code of zero");
+          }
+        if (kind == SC_WEIGHT_E4M3 && r < cols && !nan_codes)
+          for (int64_t c = 0; c < k; ++c)
+            if ((row[c] & 0x7Fu) == 0x7Fu) {
+              nan_codes = true;
+              break;
+            }
+      }
+    }
+    if ((s = check_cuda(ctx, cudaMalloc(&w->arena, w->bytes), "weight arena")) != SC_OK) return cleanup(s);
+    w->values = w->arena;
+    w->scales = reinterpret_cast<float*>(w->arena + soff);
+    cudaError_t e = cudaMemcpyAsync(w->values, v, vbytes, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(w->scales, sf.data(), sf.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if ((s = check_cuda(ctx, e, "arena upload")) != SC_OK) return cleanup(s);
+    w->has_nan_codes = kind == SC_WEIGHT_E4M3 && nan_codes;
+    if ((s = make_tmap_w(ctx, w)) != SC_OK) return cleanup(s);
+    *out = w;
+    return SC_OK;
+  }
   if ((s = check_cuda(ctx, cudaMalloc(&w->arena, w->bytes), "weight arena")) != SC_OK) return cleanup(s);
   w->values = w->arena;
   w->scales = reinterpret_cast<float*>(w->arena + soff);
@@ -636,7 +699,12 @@ sc_status sc_rotate_activation(sc_ctx* ctx, const sc_bf16* x, int64_t m, int64_t
 sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* bytes) {
   if (ctx == nullptr) return SC_INVALID_ARG;
   if (w == nullptr || bytes == nullptr || m < 0) return fail(ctx, SC_INVALID_ARG, "bad argument");
-  if (m >= 1 && m <= 32) *bytes = gemv_workspace_bytes(w, m, ctx->sm_count);
+  if (m > kSkinnyMinRows && m <= 32) {
+    const int grid = skinny_sk_grid(w, ctx->sm_count);
+    *bytes = grid > 0 ? skinny_sk_workspace_bytes(grid) : 0;
+  } else if (m >= 1 && m <= 32) {
+    *bytes = gemv_workspace_bytes(w, m, ctx->sm_count);
+  }
   else if (m >= kWidenMinRows) *bytes = widened_bytes(w);
   else *bytes = 0;
   if (w->rotation != 0 && m >= 1) *bytes += rotated_x_bytes(m, w->k);  // the rotated x comes first

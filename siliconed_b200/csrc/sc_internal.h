@@ -40,6 +40,15 @@ typedef CUresult (*sc_encode_tiled_fn)(CUtensorMap*, CUtensorMapDataType, cuuint
                                        const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                        CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// A set of device counters that every launch using them returns to zero, and the stream and completion
+// event of the last launch that used them: a product on another stream while that launch may still run
+// takes a route without them (sc_abi.cu, counters_free).
+struct sc_counter_guard {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t event = nullptr;
+  bool launched = false;
+};
+
 struct sc_ctx {
   int device = -1;
   int sm_count = 0;
@@ -50,11 +59,11 @@ struct sc_ctx {
   // The fused widening's readiness counters (kWidenCounterWords, then the CTA exit count), zeroed at
   // creation; every launch that uses them returns them to zero as its last CTA leaves.
   uint32_t* d_widen = nullptr;
-  // The stream of the last launch that used them and an event recorded after it: a product on another
-  // stream that would use them while that launch may still run takes the separate widening instead.
-  cudaStream_t fw_stream = nullptr;
-  cudaEvent_t fw_event = nullptr;
-  bool fw_launched = false;
+  sc_counter_guard widen_guard;
+  // The streamed skinny product's tile counters (kSkinnyCounterWords), zeroed at creation; the last CTA of
+  // each tile returns its counter to zero.
+  uint32_t* d_skinny = nullptr;
+  sc_counter_guard skinny_guard;
   // sc_linear_host's copy streams and events, created on its first call and kept with the context.
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
   cudaEvent_t host_events[2 * 32 + 2] = {};
@@ -194,6 +203,15 @@ cudaError_t launch_gemm_skinny(const CUtensorMap& tmap_x, const sc_weight* w, co
                                bool f32_out, int64_t m, int* err, int sm_count, cudaStream_t stream);
 // Rows above which sc_linear leaves the GEMV for the skinny tensor-core product.
 constexpr int64_t kSkinnyMinRows = 4;
+// The skinny product streamed in equal shares over one CTA per SM (sc_gemm_skinny_sk.cu): its grid for a
+// weight (0: the cluster kernel above serves it), its workspace (the tiles' fp32 partials), and the launch
+// (counters: the context's kSkinnyCounterWords tile counters, zero between launches).
+constexpr int kSkinnyCounterWords = 8192;
+int skinny_sk_grid(const sc_weight* w, int sm_count);
+size_t skinny_sk_workspace_bytes(int grid);
+cudaError_t launch_gemm_skinny_sk(const CUtensorMap& tmap_x, const sc_weight* w, const uint16_t* bias, void* y,
+                                  bool f32_out, int64_t m, float* partials, uint32_t* counters, int grid, int* err,
+                                  cudaStream_t stream);
 
 // CTA count and workspace of the skinny product.
 int gemv_splits(const sc_weight* w, int64_t m, int sm_count);

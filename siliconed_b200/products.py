@@ -104,10 +104,14 @@ class QuantizedWeight:
     values: [K, N] codes in the map's layout (or [N, K] with ``published_nk``), int8 / uint8 bytes, as a
     numpy array or a torch tensor (CPU or CUDA).  scales: one per output (shape [N]) or one for the
     tensor (shape [] / [1]), fp32 / bf16 / fp16.  ``columns=(n0, n1)`` keeps only that column shard.
+    ``arena=(k, n)``: values are the arena's own [n_pad][k_pad] bytes of a [K, N] weight (a map stored
+    re-tiled), registered with one copy (SC_WEIGHT_ARENA_LAYOUT); ``nan_codes`` states that device-resident
+    e4m3 codes hold NaN codes (host codes are scanned by the library).
     """
 
     def __init__(self, ctx: Context, values, kind: int, scales, *, scale_type: int | None = None,
-                 published_nk: bool = False, columns: tuple[int, int] | None = None, rotation: int = 0, stream=None):
+                 published_nk: bool = False, columns: tuple[int, int] | None = None, rotation: int = 0, stream=None,
+                 arena: tuple[int, int] | None = None, nan_codes: bool = False):
         self.ctx = ctx
         lib = ctx.lib
         on_device = torch is not None and isinstance(values, torch.Tensor) and values.is_cuda
@@ -125,7 +129,12 @@ class QuantizedWeight:
             shape = v.shape
         if len(shape) != 2:
             raise SiliconedError(abi.INVALID_ARG, "values must be 2-D")
-        k, n = (shape[1], shape[0]) if published_nk else shape
+        if arena is not None:
+            k, n = (int(arena[0]), int(arena[1]))
+            if tuple(shape) != (-(-n // 256) * 256, -(-k // 64) * 64) or published_nk or columns is not None:
+                raise SiliconedError(abi.INVALID_ARG, f"arena values of [{k}, {n}] are [n_pad, k_pad] bytes, whole")
+        else:
+            k, n = (shape[1], shape[0]) if published_nk else shape
         st, s = _scale_type_of(scales, scale_type)
         if scale_type is not None:
             st = scale_type
@@ -137,6 +146,8 @@ class QuantizedWeight:
         if on_device != s_on_device:
             s = s.to(values.device) if on_device else (s.cpu() if isinstance(s, torch.Tensor) else s)
         flags = (abi.VALUES_ON_DEVICE if on_device else 0) | (abi.PUBLISHED_NK if published_nk else 0)
+        if arena is not None:
+            flags |= abi.ARENA_LAYOUT | (abi.NAN_CODES if nan_codes else 0)
         n0, n1 = columns if columns is not None else (0, n)
         p = ctypes.c_void_p()
         self._keep = (v, s)

@@ -13,7 +13,7 @@ import os
 import numpy as np
 import pytest
 
-from siliconed_b200 import artifact
+from siliconed_b200 import artifact, configs
 from siliconed_b200.artifact import Artifact, MapError, MapTensor, element_count, header_length
 
 INT_MAX = (1 << 63) - 1
@@ -285,3 +285,62 @@ def test_the_forge_refuses_what_the_reference_refuses():
     assert artifact.forge_linear("a.weight", q, np.zeros(2, np.float32), "int8", "float32").scale_shape == (2,)
     cast = artifact.forge_linear("c.weight", q, None, "float8_e4m3", None)
     assert cast.scale is None and cast.shape == (4, 2) and cast.total_bytes() == 8
+
+
+def test_a_linear_stored_in_the_arena_layout_round_trips(tmp_path):
+    """The re-tiled map (this library's extension, ``"layout": "arena"``): the codes stored as the device
+    arena keeps them, [n_pad][k_pad] with int8 biased and the padding the code of zero, computed here
+    independently; the reader gives back the published [K, N] codes and the scale as published."""
+    rng = np.random.default_rng(5)
+    qi = rng.integers(-128, 128, (300, 200), dtype=np.int16).astype(np.int8)         # [N, K]
+    si = configs.to_bf16_bits((np.abs(rng.standard_normal((300, 1))) * 1e-3 + 1e-5).astype(np.float32))
+    qe = configs.to_e4m3_codes(rng.standard_normal((70, 128), dtype=np.float32) * 8)
+    qe[3, 5] = 0x7F                                                                   # a NaN code
+    se = np.array([0.5], np.float32)
+    ts = [artifact.forge_linear("i.weight", qi, si, "int8", "bfloat16", layout="arena"),
+          artifact.forge_linear("e.weight", qe, se, "float8_e4m3", "float32", layout="arena"),
+          artifact.forge_linear("r.weight", qi[:, :192], si, "int8", "bfloat16", rotation=64, layout="arena")]
+    path = str(tmp_path / "arena.silicon")
+    artifact.write_map(path, ts)
+    with artifact.Artifact(path) as a:
+        t = a.tensor("i.weight")
+        assert t.layout == "arena" and t.shape == (200, 300) and not t.nan_codes
+        want = np.full((512, 256), 0x80, np.uint8)
+        want[:300, :200] = qi.view(np.uint8) ^ 0x80
+        assert np.array_equal(a.stored("i.weight"), want)
+        assert t.scale.offset == 512 * 256 and t.bytes == 512 * 256 + 600
+        assert np.array_equal(a.values("i.weight"), qi.view(np.uint8).T)
+        assert np.array_equal(a.scale_values("i.weight")[1].reshape(-1), si.reshape(-1))
+        e = a.tensor("e.weight")
+        assert e.nan_codes and e.scale.shape == ()
+        want = np.zeros((256, 128), np.uint8)
+        want[:70] = qe
+        assert np.array_equal(a.stored("e.weight"), want)
+        assert np.array_equal(a.values("e.weight"), qe.T)
+        r = a.tensor("r.weight")
+        assert r.rotation.group == 64 and r.layout == "arena"
+        assert np.array_equal(a.values("r.weight"), qi[:, :192].view(np.uint8).T)
+
+
+def test_the_arena_layout_is_checked(tmp_path):
+    rng = np.random.default_rng(6)
+    q = rng.integers(-128, 128, (40, 64), dtype=np.int16).astype(np.int8)
+    t = artifact.forge_linear("w", q, np.full(40, 1e-3, np.float32), "int8", "float32", layout="arena")
+    good = str(tmp_path / "good.silicon")
+    artifact.write_map(good, [t])
+    raw = bytearray(open(good, "rb").read())
+    n = int.from_bytes(raw[8:16], "little")
+    header = json.loads(raw[16:16 + n])
+    for change in ({"layout": "tiled"}, {"dtype": "bfloat16"}, {"bytes": header["tensors"]["w"]["bytes"] - 16},
+                   {"nan_codes": 1}):
+        h = json.loads(json.dumps(header))
+        h["tensors"]["w"].update(change)
+        text = json.dumps(h).encode()
+        bad = str(tmp_path / "bad.silicon")
+        with open(bad, "wb") as f:
+            f.write(raw[:8] + len(text).to_bytes(8, "little") + text + bytes(header["data_start"] - 16 - len(text))
+                    + raw[header["data_start"]:])
+        with pytest.raises(artifact.MapError):
+            artifact.Artifact(bad)
+    with pytest.raises(artifact.ForgeRefusal):
+        artifact.forge_linear("w", q, np.full(40, 1e-3, np.float32), "int8", "float32", layout="tiled")

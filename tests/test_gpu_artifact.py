@@ -111,3 +111,47 @@ def test_a_forged_map_registers_in_place(ctx, tmp_path):
         w.close()
     products.close()
     m.close()
+
+
+def test_a_map_stored_in_the_arena_layout_registers_with_one_copy(ctx, tmp_path):
+    """The same published weights forged in the map's [K, N] layout and in the arena layout (the codes
+    re-tiled at forge time, registration one copy, no re-tiling kernel): identical exports and identical
+    product bits, for int8 with bf16 row scales, e4m3 holding NaN codes, and int8 convrot; a stored
+    padding byte that is not the code of zero is refused at registration."""
+    rng = np.random.default_rng(21)
+    q1 = rng.integers(-128, 128, (600, 1024), dtype=np.int16).astype(np.int8)
+    s1 = configs.to_bf16_bits((np.abs(rng.standard_normal((600, 1))) * 0.02 / 127 + 1e-5).astype(np.float32))
+    q2 = configs.to_e4m3_codes(rng.standard_normal((300, 512), dtype=np.float32) * 8)
+    q2[rng.integers(0, 300, 5), rng.integers(0, 512, 5)] = 0x7F
+    s2 = (np.abs(rng.standard_normal(300)) * 0.02 / 448 + 1e-5).astype(np.float32)
+    q3 = rng.integers(-128, 128, (264, 512), dtype=np.int16).astype(np.int8)
+    s3 = (np.abs(rng.standard_normal(264)) * 0.02 / 127 + 1e-5).astype(np.float32)
+    specs = [("a.weight", q1, s1, "int8", "bfloat16", None), ("b.weight", q2, s2, "float8_e4m3", "float32", None),
+             ("c.weight", q3, s3, "int8", "float32", 256)]
+    maps = {}
+    for layout in (None, "arena"):
+        ts = [artifact.forge_linear(n, q, s, d, sd, rotation=r, layout=layout) for n, q, s, d, sd, r in specs]
+        path = str(tmp_path / f"{layout}.silicon")
+        artifact.write_map(path, ts)
+        maps[layout] = artifact.Artifact(path)
+    for name, q, *_ in specs:
+        plain, arena = maps[None].register(ctx, name), maps["arena"].register(ctx, name)
+        assert canonical(plain.dequantize().cpu().numpy()).tobytes() == canonical(arena.dequantize().cpu().numpy()).tobytes()
+        for m in (3, 200, 1600):
+            x = bf16_dev(configs.to_bf16_bits(rng.standard_normal((m, plain.k), dtype=np.float32)))
+            a, b = plain.linear(x), arena.linear(x)
+            torch.cuda.synchronize()
+            assert canonical(a.float().cpu().numpy()).tobytes() == canonical(b.float().cpu().numpy()).tobytes(), (name, m)
+        plain.close()
+        arena.close()
+    for m in maps.values():
+        m.close()
+    # a K padding byte that is not the code of zero: refused before anything is uploaded
+    t = artifact.forge_linear("w", q1[:, :1000], s1, "int8", "bfloat16", layout="arena")
+    t.data[0, 1010] = 0x81
+    bad = str(tmp_path / "bad.silicon")
+    artifact.write_map(bad, [t])
+    with artifact.Artifact(bad) as a:
+        with pytest.raises(abi.SiliconedError) as e:
+            a.register(ctx, "w")
+        assert e.value.status == abi.INVALID_ARG

@@ -252,6 +252,41 @@ def test_skinny_tensor_core_product_agrees_with_gemv(ctx, kind, m, nan):
     w.close()
 
 
+@pytest.mark.parametrize("kind,m,k,n", [(abi.WEIGHT_INT8, 16, 4096, 12288), (abi.WEIGHT_INT8, 32, 12288, 4096),
+                                         (abi.WEIGHT_E4M3, 7, 1024, 4000), (abi.WEIGHT_INT8, 9, 256, 38400)])
+def test_streamed_skinny_product_matches_the_oracle_and_repeats(ctx, kind, m, k, n):
+    """With its workspace, 4 < m <= 32 streams the weight in equal shares over one CTA per SM (a share
+    crosses tiles: the last of K = 256's shares span three); the tiles' partials meet in K order.  fp32
+    output within the oracle's bar, the same bits on a second call, and within the bar of the cluster
+    kernel that runs without the workspace."""
+    g = np.random.default_rng(m * k + n)
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    if kind == abi.WEIGHT_INT8:
+        q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+    else:
+        q = configs.to_e4m3_codes(g.standard_normal((k, n), dtype=np.float32) * 4)
+        q[(q & 0x7F) == 0x7F] ^= 1
+    s = (np.abs(g.standard_normal(n)) * 0.01 / 127 + 1e-6).astype(np.float32)
+    b = configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.01)
+    w = QuantizedWeight(ctx, q, kind, s)
+    assert w.workspace_bytes(m) > 0, "the streamed route applies"
+    xd, bd = bf16_dev(x), bf16_dev(b)
+    if kind == abi.WEIGHT_INT8:
+        c_ref, y_ref = oracle.linear_int8(x, q.view(np.int8), s, b)
+    else:
+        wf = oracle.dequantize(q, oracle.E4M3, s, oracle.SCALE_F32, oracle.LAYOUT_COLUMNS, n).reshape(k, n)
+        c_ref, y_ref = oracle.linear_widened(x, wf, b)
+    first = host(linear_ex(ctx, w, xd, m, bd, True))
+    again = host(linear_ex(ctx, w, xd, m, bd, True))
+    cluster = host(linear_ex(ctx, w, xd, m, bd, True, workspace=False))
+    assert rel_l2(first, c_ref) <= REL_L2_F32, rel_l2(first, c_ref)
+    assert np.array_equal(first.view(np.uint32), again.view(np.uint32)), "the same bits on a second call"
+    assert rel_l2(cluster, first) <= REL_L2_F32
+    y16 = f32_of_bf16(bf16_host(linear_ex(ctx, w, xd, m, bd, False)))
+    assert rel_l2(y16, f32_of_bf16(y_ref)) <= REL_L2_BF16
+    w.close()
+
+
 def test_gemv_meets_the_reference_bar(ctx):
     """Qwen3VLDecoderTests.swift:250-263 on its own inputs (x rounded to bf16): per-channel relative
     L2 against fp64, median < 1e-6 and worst < 5e-6, for every scale type."""
