@@ -154,13 +154,14 @@ sc_status make_tmap_w(sc_ctx* ctx, sc_weight* w) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w->k_pad), static_cast<cuuint64_t>(w->n_pad)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w->k_pad)};
   const cuuint32_t estr[2] = {1, 1};
-  CUtensorMap* maps[2] = {&w->tmap_values, &w->tmap_values_half};
-  const cuuint32_t rows[2] = {256, 128};
-  for (int i = 0; i < 2; ++i) {
-    const cuuint32_t box[2] = {64, rows[i]};
+  CUtensorMap* maps[3] = {&w->tmap_values, &w->tmap_values_half, &w->tmap_values_wide};
+  const cuuint32_t inner[3] = {64, 64, 128}, rows[3] = {256, 128, 128};
+  const CUtensorMapSwizzle swz[3] = {CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_SWIZZLE_128B};
+  for (int i = 0; i < 3; ++i) {
+    const cuuint32_t box[2] = {inner[i], rows[i]};
     CUresult r = ctx->encode_tiled(maps[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->values, dims, strides, box, estr,
-                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz[i], CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
       return fail(ctx, SC_CUDA_ERROR, "cuTensorMapEncodeTiled (weights) failed: " + std::to_string(r));
   }
@@ -263,18 +264,20 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
   CUtensorMap tmx;
   if (m <= 32) {
     if ((s = make_tmap_x(ctx, x, m, w->k, &tmx, gemm_skinny_box_rows(m))) != SC_OK) return s;
-    // With the workspace for the tiles' partials: every SM streams an equal share of the weight.  Without
-    // it: the cluster kernel, whose K parts meet in distributed shared memory.
-    const int grid = skinny_sk_grid(w, ctx->sm_count);
-    bool streamed = false;
-    if (grid > 0 && workspace != nullptr && workspace_bytes >= skinny_sk_workspace_bytes(grid) &&
+    // int8, m <= 16, with the workspace for x's digit planes and the tiles' partials: the codes straight into
+    // the integer tensor cores, every SM an equal share of the weight.  Otherwise (e4m3, m > 16, or no
+    // workspace): the cluster kernel, which converts the codes to bf16 and adds its K parts in distributed
+    // shared memory.
+    const int grid = skinny_i8_grid(w, m, ctx->sm_count);
+    bool integer = false;
+    if (grid > 0 && workspace != nullptr && workspace_bytes >= skinny_i8_workspace_bytes(w, m, grid) &&
         (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0 &&
-        (s = counters_free(ctx, ctx->skinny_guard, st, streamed)) != SC_OK)
+        (s = counters_free(ctx, ctx->skinny_guard, st, integer)) != SC_OK)
       return s;
-    if (streamed) {
-      if ((s = check_cuda(ctx, launch_gemm_skinny_sk(tmx, w, bias, y, f32_out, m, static_cast<float*>(workspace),
+    if (integer) {
+      if ((s = check_cuda(ctx, launch_gemm_skinny_i8(ctx->encode_tiled, x, w, bias, y, f32_out, m, workspace,
                                                      ctx->d_skinny, grid, ctx->d_err, st),
-                          "streamed skinny gemm launch")) != SC_OK)
+                          "int8 skinny gemm launch")) != SC_OK)
         return s;
       return counters_launched(ctx, ctx->skinny_guard, st);
     }
@@ -700,8 +703,8 @@ sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* 
   if (ctx == nullptr) return SC_INVALID_ARG;
   if (w == nullptr || bytes == nullptr || m < 0) return fail(ctx, SC_INVALID_ARG, "bad argument");
   if (m > kSkinnyMinRows && m <= 32) {
-    const int grid = skinny_sk_grid(w, ctx->sm_count);
-    *bytes = grid > 0 ? skinny_sk_workspace_bytes(grid) : 0;
+    const int grid = skinny_i8_grid(w, m, ctx->sm_count);
+    *bytes = grid > 0 ? skinny_i8_workspace_bytes(w, m, grid) : 0;
   } else if (m >= 1 && m <= 32) {
     *bytes = gemv_workspace_bytes(w, m, ctx->sm_count);
   }

@@ -1,21 +1,30 @@
-// The skinny product (4 < m <= 32) streamed in equal shares: every SM reads the same number of weight
-// bytes, however N and K fall into tiles.
+// The int8 skinny product (4 < m <= 16) on the integer tensor cores, the codes read as stored.
 //
-// The work is the list of units (column tile t of 128 outputs, 64-wide K stage kt), tile-major, split
-// evenly over one CTA per SM: CTA c takes units [c U / G, (c + 1) U / G).  Its share crosses at most a
-// few tiles; each run of units inside one tile is a segment, summed in TMEM in K order.  A segment that
-// covers its whole tile writes y directly.  Otherwise its fp32 partial goes to the caller's workspace and
-// the CTA counts itself on the tile's counter (the context's, returned to zero by the last CTA of the
-// tile); the last CTA adds the tile's partials in K order (fragment by fragment, whichever CTA arrives
-// last), so every run gives the same bits.
+// Converting every code to bf16 before a kind::f16 MMA is what bounds a skinny product: the conversion runs
+// on the CUDA cores at one pass per 64-code sub-tile, and on B200 it held both skinny designs to about
+// 0.9 us per 8 KB of codes per SM (33-39 us for config 4's 50 MB weight) with the tensor pipe 3 % busy.
+// Here the codes never change form.  Each row of x (bf16) is first written as an exact fixed-point
+// integer v = round(x * 2^(21 - e)), e the row's largest exponent (|v| < 2^22: every value whose exponent
+// is within 14 of the row's largest is exact, the rest are rounded at 2^-22 of the largest, finer than an
+// fp32 sum keeps), split into three signed 8-bit digits v = d0 + 2^8 d1 + 2^16 d2 (x_planes).  The product
+// then multiplies the arena's biased codes u = q + 128 (unsigned 8-bit, A) by the digit planes (signed 8-bit,
+// B, the 3 MT rows of one MMA of N = 3 MT) with tcgen05.mma kind::i8 into s32 accumulators: sum_d 2^(8d)
+// acc_d = sum_k v_k u_k exactly, and subtracting 128 sum_k v_k leaves sum_k v_k q_k, an exact integer.  The
+// epilogue turns it into the fp32 sum with one rounding (times 2^(e - 21), exact), then applies the scale
+// and the bias as the native route does.  The sum is exact where the fp32 route rounds at every step, so
+// the results agree with the oracle's fp32 sums to within their rounding.
 //
-// Per unit, as in the cluster kernel (sc_gemm_skinny.cu): TMA brings x's tile (bf16 [MT x 64], 128-byte
-// swizzle) and the codes' tile (bytes [128 x 64]); 8 converter warps decode the codes exactly to the
-// swizzled bf16 layout; one thread issues four tcgen05.mma kind::f16 (M 128 weight columns, N MT tokens,
-// K 16).  The ring holds 12 units (96 KB of codes in flight per SM), and the first 12 code tiles are
-// requested before the CTA waits for the kernel ahead of it (programmatic dependent launch): in a decode
-// step that kernel produced x, while the codes depend on nothing.  Two TMEM accumulators let a segment's
-// epilogue overlap the next segment's MMAs.  No load uses cluster multicast; every wait is bounded.
+// The work is the list of units (column tile t of 128 outputs, 256-wide K chunk kt), tile-major, split
+// evenly over one CTA per SM: CTA c takes units [c U / G, (c + 1) U / G), so every SM reads the same
+// number of weight bytes.  Its share crosses at most a few tiles; each run of units inside one tile is a
+// segment, summed in TMEM.  A segment that covers its whole tile writes y directly.  Otherwise its integer
+// partial (int64, exact) goes to the caller's workspace and the CTA counts itself on the tile's counter
+// (the context's, returned to zero by the tile's last CTA); the last CTA adds the tile's partials, exactly,
+// so every run gives the same bits.  Per unit, TMA brings the codes as two 16 KB boxes (128 bytes x 128
+// rows, 128-byte swizzle: the MMA's operand layout as stored) and the planes as two [3 MT x 128] boxes; a
+// ring of 5 units keeps 160 KB of codes in flight per SM, the first ones requested
+// before the CTA waits for the kernel ahead of it (programmatic dependent launch).  No load uses cluster
+// multicast; every wait is bounded.
 #include <cuda_bf16.h>
 
 #include "sc_codes.cuh"
@@ -23,32 +32,27 @@
 #include "sc_ptx.cuh"
 
 namespace sc {
-namespace skinny_sk {
+namespace skinny_i8 {
 
-constexpr int BN = 128, BK = 64;
-constexpr int kStagesIn = 12;
-constexpr int kStagesB = 3;
-constexpr int kWBytes = BN * BK;
-constexpr int kBBytes = BN * BK * 2;
-constexpr int kMaxTokens = 32;
-constexpr int kXBytesMax = kMaxTokens * BK * 2;
-constexpr int kWarps = 16, kThreads = kWarps * 32;
+constexpr int BN = 128;                 // weight columns per tile (the MMA's M)
+constexpr int BKU = 256;                // K of a unit: two 128-byte boxes
+constexpr int kBoxBytes = BN * 128;     // 16 KB
+constexpr int kCodeBytes = 2 * kBoxBytes;
+constexpr int kTokens = 16;            // x rows a launch takes (m <= 16; the rows past m are zeros)
+constexpr int kStages = 5;             // ring depth: 5 units, 160 KB of codes and 60 KB of planes
+constexpr int kWarps = 8, kThreads = kWarps * 32;
 constexpr int kEpiWarp0 = 4, kEpiWarps = 4;
-constexpr int kConvWarp0 = 8, kConvWarps = 8, kConvThreads = kConvWarps * 32;
-constexpr int kChunksPerStage = BN * BK / 16;
-constexpr uint32_t kTmemCols = 64;  // two accumulators of 32 columns
-constexpr int kMaxSegments = 4;     // tiles a CTA's share may cross (the host checks)
+constexpr uint32_t kTmemCols = 256;     // two accumulators of 3 MT columns, 128 apart
+constexpr int kSlots = 2;               // partial slots per CTA: its first and its last segment
+constexpr int kZeroRow = -100000;       // x_planes' exponent of a row of zeros
+constexpr int kBadRow = 100000;         // ... of a row holding an infinity or a NaN
 
-static_assert(kChunksPerStage % kConvThreads == 0, "converter work must divide evenly");
-
+template <int MT>
 struct __align__(1024) Smem {
-  uint8_t b[kStagesB][kBBytes];         // converted weight tiles (the MMA's A), swizzled
-  uint8_t a[kStagesIn][kXBytesMax];     // x tiles (the MMA's B), swizzled (TMA)
-  uint8_t w[kStagesIn][kWBytes];        // code tiles (TMA)
-  uint64_t in_full[kStagesIn];
-  uint64_t in_empty[kStagesIn];
-  uint64_t b_full[kStagesB];
-  uint64_t b_empty[kStagesB];
+  uint8_t w[kStages][kCodeBytes];           // codes: [2][128 rows][128 bytes], 128-byte swizzled (TMA)
+  uint8_t p[kStages][2][3 * MT * 128];      // planes: [2][3 MT rows][128 bytes], 128-byte swizzled (TMA)
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t drain;
@@ -57,7 +61,99 @@ struct __align__(1024) Smem {
   int last;  // the fix-up decision of the current segment, for the epilogue warps
 };
 
-constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+template <int MT>
+constexpr size_t smem_bytes() { return sizeof(Smem<MT>) + 1024; }
+static_assert(smem_bytes<kTokens>() <= 227 * 1024, "shared memory per CTA");
+
+// ---- x_planes: one CTA per token row (MT of them, rows past m all zero) ----------------------------
+// planes [3 MT][k_pad] int8 (row d MT + t: digit d of token t), shift[t] = e - 148 (the power of two of
+// v's unit, e the row's largest biased bf16 exponent; kZeroRow / kBadRow for a row of zeros / with a
+// non-finite value), corr[t] = 128 sum_k v_k.  Each thread takes 8 consecutive values (16-byte loads, 8-byte
+// stores per plane); k_pad is a multiple of 64 and K of 8.
+constexpr int kPlaneThreads = 1024;
+
+__device__ __forceinline__ int fixed_point(uint32_t b, int E) {
+  const int e = (b >> 7) & 0xFF;
+  if (e == 0) return 0;                                 // zero (and subnormal: below every kept digit)
+  const int a = static_cast<int>(128u | (b & 0x7Fu));   // the significand, 8 bits
+  const int sh = e - E + 14;                            // v = a * 2^sh
+  int mag;
+  if (sh >= 0) {
+    mag = a << sh;                                      // sh <= 14: below 2^22
+  } else {
+    const int r = -sh;                                  // round to nearest, ties to even
+    mag = r >= 31 ? 0 : (a >> r) + ((((a >> (r - 1)) & 1) && ((a & ((1 << (r - 1)) - 1)) || ((a >> r) & 1))) ? 1 : 0);
+  }
+  return (b & 0x8000u) ? -mag : mag;
+}
+
+__global__ void __launch_bounds__(kPlaneThreads)
+    x_planes(const uint16_t* __restrict__ x, int M, int K, int k_pad, int MT, int8_t* __restrict__ planes,
+             int* __restrict__ shift, long long* __restrict__ corr) {
+  pdl_launch_dependents();  // the product may launch and request its codes now
+  pdl_wait();               // x is the kernel ahead's output
+  __shared__ int s_max;
+  __shared__ unsigned long long s_sum;
+  const int t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    s_max = 0;
+    s_sum = 0ull;
+  }
+  __syncthreads();
+  const uint4* row = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * K);
+  const int chunks = K / 8, pad_chunks = k_pad / 8;
+  int e_max = 0;
+  if (t < M)
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+      const uint4 v = __ldg(row + c);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) e_max = max(e_max, max((w[i] >> 7) & 0xFF, (w[i] >> 23) & 0xFF));
+    }
+  e_max = static_cast<int>(__reduce_max_sync(0xFFFFFFFFu, static_cast<unsigned>(e_max)));
+  if ((threadIdx.x & 31) == 0) atomicMax(&s_max, e_max);  // one shared atomic per warp
+  __syncthreads();
+  const int E = s_max;
+  long long sum = 0;
+  uint2* p0 = reinterpret_cast<uint2*>(planes + static_cast<int64_t>(t) * k_pad);
+  uint2* p1 = reinterpret_cast<uint2*>(planes + static_cast<int64_t>(MT + t) * k_pad);
+  uint2* p2 = reinterpret_cast<uint2*>(planes + static_cast<int64_t>(2 * MT + t) * k_pad);
+  for (int c = threadIdx.x; c < pad_chunks; c += blockDim.x) {
+    uint32_t w[4] = {0, 0, 0, 0};
+    if (t < M && c < chunks && E < 255) {
+      const uint4 v = __ldg(row + c);
+      w[0] = v.x;
+      w[1] = v.y;
+      w[2] = v.z;
+      w[3] = v.w;
+    }
+    uint32_t d0[2] = {0, 0}, d1[2] = {0, 0}, d2[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t b = (w[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+      const int v = fixed_point(b, E);
+      sum += v;
+      const int g0 = ((v + 128) & 255) - 128;
+      const int v1 = (v - g0) >> 8;
+      const int g1 = ((v1 + 128) & 255) - 128;
+      const int g2 = (v1 - g1) >> 8;
+      d0[i >> 2] |= (static_cast<uint32_t>(g0) & 0xFFu) << (8 * (i & 3));
+      d1[i >> 2] |= (static_cast<uint32_t>(g1) & 0xFFu) << (8 * (i & 3));
+      d2[i >> 2] |= (static_cast<uint32_t>(g2) & 0xFFu) << (8 * (i & 3));
+    }
+    p0[c] = make_uint2(d0[0], d0[1]);
+    p1[c] = make_uint2(d1[0], d1[1]);
+    p2[c] = make_uint2(d2[0], d2[1]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+  if ((threadIdx.x & 31) == 0) atomicAdd(&s_sum, static_cast<unsigned long long>(sum));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    corr[t] = 128ll * static_cast<long long>(s_sum);
+    shift[t] = t >= M || E == 0 ? kZeroRow : (E == 255 ? kBadRow : E - 148);
+  }
+}
 
 // The CTA whose share holds unit u: the largest c with floor(c U / G) <= u.
 __device__ __forceinline__ int owner(int64_t u, int64_t units, int grid) {
@@ -67,30 +163,28 @@ __device__ __forceinline__ int owner(int64_t u, int64_t units, int grid) {
 
 __device__ __forceinline__ int64_t share_begin(int c, int64_t units, int grid) { return c * units / grid; }
 
-template <int kKind, bool kNaN, bool kF32Out, int MT>
+template <bool kF32Out, int MT>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_w8_skinny_sk(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                      const float* __restrict__ scales, const uint16_t* __restrict__ bias, void* __restrict__ y_out,
-                      int M, int N, int k_tiles, int n_tiles, float* __restrict__ partials,
-                      uint32_t* __restrict__ counters, int* err) {
+    gemm_i8_skinny(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_p,
+                   const float* __restrict__ scales, const uint16_t* __restrict__ bias, void* __restrict__ y_out,
+                   int M, int N, int k_tiles, int n_tiles, const int* __restrict__ shift,
+                   const long long* __restrict__ corr, long long* __restrict__ partials,
+                   uint32_t* __restrict__ counters, int* err) {
+  constexpr int kRows = 3 * MT;                // the MMA's N: three digit planes of MT tokens
+  constexpr int kPlaneBox = kRows * 128;
   extern __shared__ uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Smem<MT>& s = *reinterpret_cast<Smem<MT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grid = static_cast<int>(gridDim.x);
   const int64_t units = static_cast<int64_t>(n_tiles) * k_tiles;
   const int64_t u0 = share_begin(blockIdx.x, units, grid), u1 = share_begin(blockIdx.x + 1, units, grid);
-  constexpr int kXBytes = MT * BK * 2;
   volatile int* abort = &s.abort;
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStagesIn; ++i) {
-      mbar_init(&s.in_full[i], 1);
-      mbar_init(&s.in_empty[i], 1 + kConvWarps);  // the MMA's commit + one per converter warp
-    }
-    for (int i = 0; i < kStagesB; ++i) {
-      mbar_init(&s.b_full[i], kConvWarps);
-      mbar_init(&s.b_empty[i], 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full[i], 1);
@@ -99,8 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&s.drain, 1);
     s.abort = 0;
     fence_mbar_init();
-    prefetch_tensormap(&tm_x);
     prefetch_tensormap(&tm_w);
+    prefetch_tensormap(&tm_p);
   }
   if (warp == 1) {
     tmem_alloc(&s.tmem_base, kTmemCols);
@@ -114,76 +208,80 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0, issued = 0, last_parity = 0;
-      const int pre = static_cast<int>(u1 - u0 < kStagesIn ? u1 - u0 : kStagesIn);
-      // the first code tiles do not depend on the kernel ahead: requested before waiting for it
+      const int pre = static_cast<int>(u1 - u0 < kStages ? u1 - u0 : kStages);
+      auto unit_of = [&](int64_t u, int& t, int& kt) {
+        t = static_cast<int>(u / k_tiles);
+        kt = static_cast<int>(u - static_cast<int64_t>(t) * k_tiles);
+      };
+      // the first units' codes do not depend on the kernels ahead: requested before waiting for them
       for (int i = 0; i < pre; ++i) {
-        const int64_t u = u0 + i;
-        const int t = static_cast<int>(u / k_tiles), kt = static_cast<int>(u - static_cast<int64_t>(t) * k_tiles);
-        mbar_arrive_expect_tx(&s.in_full[i], kXBytes + kWBytes);
-        tma_load_2d(s.w[i], &tm_w, &s.in_full[i], kt * BK, t * BN);
+        int t, kt;
+        unit_of(u0 + i, t, kt);
+        mbar_arrive_expect_tx(&s.full[i], kCodeBytes + 2 * kPlaneBox);
+        tma_load_2d(s.w[i], &tm_w, &s.full[i], kt * BKU, t * BN);
+        tma_load_2d(s.w[i] + kBoxBytes, &tm_w, &s.full[i], kt * BKU + 128, t * BN);
       }
-      pdl_wait();
+      pdl_wait();  // the planes are the kernel ahead's output
+      uint32_t issued = 0, last_parity = 0;
       for (int i = 0; i < pre; ++i) {
-        const int64_t u = u0 + i;
-        const int t = static_cast<int>(u / k_tiles), kt = static_cast<int>(u - static_cast<int64_t>(t) * k_tiles);
-        tma_load_2d(s.a[i], &tm_x, &s.in_full[i], kt * BK, 0);
+        int t, kt;
+        unit_of(u0 + i, t, kt);
+        tma_load_2d(s.p[i][0], &tm_p, &s.full[i], kt * BKU, 0);
+        tma_load_2d(s.p[i][1], &tm_p, &s.full[i], kt * BKU + 128, 0);
         issued |= 1u << i;
-        last_parity &= ~(1u << i);
       }
-      stage = pre % kStagesIn;
-      phase = pre == kStagesIn ? 1u : 0u;
+      int stage = pre % kStages;
+      uint32_t phase = pre == kStages ? 1u : 0u;
       for (int64_t u = u0 + pre; u < u1 && !*abort; ++u) {
-        if (!mbar_wait(&s.in_empty[stage], phase ^ 1u, abort, err, kSiteProducerEmpty)) break;
-        const int t = static_cast<int>(u / k_tiles), kt = static_cast<int>(u - static_cast<int64_t>(t) * k_tiles);
-        mbar_arrive_expect_tx(&s.in_full[stage], kXBytes + kWBytes);
-        tma_load_2d(s.w[stage], &tm_w, &s.in_full[stage], kt * BK, t * BN);
-        tma_load_2d(s.a[stage], &tm_x, &s.in_full[stage], kt * BK, 0);
+        if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort, err, kSiteProducerEmpty)) break;
+        int t, kt;
+        unit_of(u, t, kt);
+        mbar_arrive_expect_tx(&s.full[stage], kCodeBytes + 2 * kPlaneBox);
+        tma_load_2d(s.w[stage], &tm_w, &s.full[stage], kt * BKU, t * BN);
+        tma_load_2d(s.w[stage] + kBoxBytes, &tm_w, &s.full[stage], kt * BKU + 128, t * BN);
+        tma_load_2d(s.p[stage][0], &tm_p, &s.full[stage], kt * BKU, 0);
+        tma_load_2d(s.p[stage][1], &tm_p, &s.full[stage], kt * BKU + 128, 0);
         issued |= 1u << stage;
         last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == kStagesIn) {
+        if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;
         }
       }
-      for (int st = 0; st < kStagesIn; ++st)
-        if (issued & (1u << st)) mbar_wait_drain(&s.in_full[st], (last_parity >> st) & 1u);
+      for (int st = 0; st < kStages; ++st)
+        if (issued & (1u << st)) mbar_wait_drain(&s.full[st], (last_parity >> st) & 1u);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16(BN, MT);
-      int stage = 0, bstage = 0, acc = 0;
-      uint32_t phase = 0, bphase = 0, acc_phase = 0;
+      const uint32_t idesc = umma_idesc_u8s8(BN, kRows);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       for (int64_t u = u0; u < u1 && ok;) {
         const int t = static_cast<int>(u / k_tiles);
         const int64_t seg_end = u1 < static_cast<int64_t>(t + 1) * k_tiles ? u1 : static_cast<int64_t>(t + 1) * k_tiles;
         if (!mbar_wait(&s.acc_empty[acc], acc_phase ^ 1u, abort, err, kSiteMmaAccum)) break;
         tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(acc * 32);
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * 128);
         for (int64_t v = u; v < seg_end; ++v) {
-          if (!mbar_wait(&s.in_full[stage], phase, abort, err, kSiteMmaInput) ||
-              !mbar_wait(&s.b_full[bstage], bphase, abort, err, kSiteMmaConverted)) {
+          if (!mbar_wait(&s.full[stage], phase, abort, err, kSiteMmaInput)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(s.b[bstage]), b0 = smem_u32(s.a[stage]);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            tc_mma_f16(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
-                       (v != u || kk != 0) ? 1u : 0u);
-          tc_commit(&s.in_empty[stage]);
-          tc_commit(&s.b_empty[bstage]);
-          if (++stage == kStagesIn) {
+          for (int b = 0; b < 2; ++b) {
+            const uint32_t a0 = smem_u32(s.w[stage] + b * kBoxBytes), b0 = smem_u32(s.p[stage][b]);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)  // K 32 a step: 32 bytes inside the swizzle atom
+              tc_mma_i8(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
+                        (v != u || b != 0 || kk != 0) ? 1u : 0u);
+          }
+          tc_commit(&s.empty[stage]);
+          if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
-          }
-          if (++bstage == kStagesB) {
-            bstage = 0;
-            bphase ^= 1u;
           }
         }
         if (!ok) break;
@@ -196,12 +294,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_drain(&s.drain, 0);
     }
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
-    // ---------------- segment epilogue: y, or a partial and the tile's fix-up ----------------
+    // ---------------- segment epilogue: y, or an integer partial and the tile's fix-up ----------------
+    pdl_wait();  // the shifts and corrections are the kernel ahead's output
     const int ew = warp - kEpiWarp0;  // TMEM lanes [32 ew, 32 ew + 32): output columns of the tile
     const int row = ew * 32 + lane;
     int acc = 0, seg = 0;
     uint32_t acc_phase = 0;
-    const int tile0 = static_cast<int>(u0 / k_tiles);
     for (int64_t u = u0; u < u1; ++seg) {
       const int t = static_cast<int>(u / k_tiles);
       const int64_t tile_end = static_cast<int64_t>(t + 1) * k_tiles;
@@ -210,17 +308,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       int got = 0;
       if (lane == 0) got = mbar_wait(&s.acc_full[acc], acc_phase, abort, err, kSiteEpilogueFull) ? 1 : 0;
       got = __shfl_sync(0xFFFFFFFFu, got, 0);
-      float v[MT];
+      long long v[MT];
+#pragma unroll
+      for (int i = 0; i < MT; ++i) v[i] = 0;
       if (got) {
         tc_fence_after();
-        uint32_t r[32];
-        tmem_ld_32(tmem + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * 32), r);
-        tmem_wait_ld();
+        const uint32_t base = tmem + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * 128);
 #pragma unroll
-        for (int i = 0; i < MT; ++i) v[i] = __uint_as_float(r[i]);
-      } else {
+        for (int c = 0; c < (kRows + 31) / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32(base + c * 32, r);
+          tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < MT; ++i) v[i] = 0.0f;
+          for (int j = 0; j < 32; ++j) {
+            const int col = c * 32 + j;
+            if (col < kRows) {
+              const int d = col / MT, tok = col % MT;
+              v[tok] += static_cast<long long>(static_cast<int>(r[j])) << (8 * d);
+            }
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -230,10 +337,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = t * BN + row;
       bool store = whole;
       if (!whole) {
-        float* mine = partials + ((static_cast<int64_t>(blockIdx.x) * kMaxSegments + seg) * BN + row) * kMaxTokens;
+        const int slot = seg == 0 ? 0 : 1;
+        long long* mine = partials + ((static_cast<int64_t>(blockIdx.x) * kSlots + slot) * BN + row) * kTokens;
 #pragma unroll
-        for (int i = 0; i < MT; i += 4)
-          *reinterpret_cast<float4*>(mine + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        for (int i = 0; i < MT; i += 2)
+          *reinterpret_cast<longlong2*>(mine + i) = make_longlong2(v[i], v[i + 1]);
         __threadfence();
         named_barrier_sync(1, kEpiWarps * 32);
         const int c_first = owner(static_cast<int64_t>(t) * k_tiles, units, grid);
@@ -248,26 +356,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         store = s.last != 0;
         if (store) {
           __threadfence();
-          // the tile's partials in K order (CTA c_first's fragment first), whichever CTA came last
 #pragma unroll
-          for (int i = 0; i < MT; ++i) v[i] = 0.0f;
-          for (int c = c_first; c <= c_last; ++c) {
-            const int cseg = t - static_cast<int>(share_begin(c, units, grid) / k_tiles);
-            const float* f = partials + ((static_cast<int64_t>(c) * kMaxSegments + cseg) * BN + row) * kMaxTokens;
+          for (int i = 0; i < MT; ++i) v[i] = 0;
+          for (int c = c_first; c <= c_last; ++c) {  // integer sums: exact in any order
+            const int cslot = t == static_cast<int>(share_begin(c, units, grid) / k_tiles) ? 0 : 1;
+            const long long* f = partials + ((static_cast<int64_t>(c) * kSlots + cslot) * BN + row) * kTokens;
 #pragma unroll
-            for (int i = 0; i < MT; i += 4) {
-              const float4 q = ld_cg_f4(f + i);
-              if (c == c_first) {
-                v[i] = q.x;
-                v[i + 1] = q.y;
-                v[i + 2] = q.z;
-                v[i + 3] = q.w;
-              } else {
-                v[i] = __fadd_rn(v[i], q.x);
-                v[i + 1] = __fadd_rn(v[i + 1], q.y);
-                v[i + 2] = __fadd_rn(v[i + 2], q.z);
-                v[i + 3] = __fadd_rn(v[i + 3], q.w);
-              }
+            for (int i = 0; i < MT; i += 2) {
+              long long a, b;
+              asm volatile("ld.global.cg.v2.s64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(f + i));
+              v[i] += a;
+              v[i + 1] += b;
             }
           }
         }
@@ -278,51 +377,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < MT; ++i)
           if (i < M) {
-            const float o = __fadd_rn(__fmul_rn(v[i], sc), b);
+            const int sh = shift[i];
+            float sum;
+            if (sh == kZeroRow) sum = 0.0f;
+            else if (sh == kBadRow) sum = __uint_as_float(0x7FC00000u);
+            else sum = static_cast<float>(ldexp(static_cast<double>(v[i] - corr[i]), sh));  // one rounding
+            const float o = __fadd_rn(__fmul_rn(sum, sc), b);
             if (kF32Out) static_cast<float*>(y_out)[static_cast<int64_t>(i) * N + n] = o;
             else static_cast<uint16_t*>(y_out)[static_cast<int64_t>(i) * N + n] = f32_to_bf16_rne(o);
           }
       }
       u = seg_end;
-    }
-    (void)tile0;
-  } else if (warp >= kConvWarp0) {
-    // ---------------- converters ----------------
-    const int ct = threadIdx.x - kConvWarp0 * 32;
-    int stage = 0, bstage = 0;
-    uint32_t phase = 0, bphase = 0;
-    for (int64_t u = u0; u < u1; ++u) {
-      if (!mbar_wait(&s.in_full[stage], phase, abort, err, kSiteConverterFull) ||
-          !mbar_wait(&s.b_empty[bstage], bphase ^ 1u, abort, err, kSiteConverterSlot))
-        break;
-      const uint8_t* src = s.w[stage];
-      uint8_t* dst = s.b[bstage];
-#pragma unroll
-      for (int i = 0; i < kChunksPerStage / kConvThreads; ++i) {
-        const int c = ct + i * kConvThreads;
-        const int r = c >> 2, kc = c & 3;  // four 16-byte chunks per 64-byte code row
-        const uint4 in = *reinterpret_cast<const uint4*>(src + r * BK + kc * 16);
-        uint4 lo, hi;
-        codes16_to_bf16<kKind, kNaN>(in, lo, hi);
-        uint8_t* drow = dst + r * (BK * 2);
-        const int sw = r & 7;
-        *reinterpret_cast<uint4*>(drow + (((2 * kc) ^ sw) << 4)) = lo;
-        *reinterpret_cast<uint4*>(drow + (((2 * kc + 1) ^ sw) << 4)) = hi;
-      }
-      fence_async_shared();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s.b_full[bstage]);
-        mbar_arrive(&s.in_empty[stage]);
-      }
-      if (++stage == kStagesIn) {
-        stage = 0;
-        phase ^= 1u;
-      }
-      if (++bstage == kStagesB) {
-        bstage = 0;
-        bphase ^= 1u;
-      }
     }
   }
 
@@ -335,64 +400,85 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int kKind, bool kNaN, bool kF32Out, int MT>
-cudaError_t launch_mt(const CUtensorMap& tm_x, const sc_weight* w, const uint16_t* bias, void* y, int64_t m,
-                      float* partials, uint32_t* counters, int grid, int* err, cudaStream_t stream) {
-  auto kernel = gemm_w8_skinny_sk<kKind, kNaN, kF32Out, MT>;
+template <bool kF32Out, int MT>
+cudaError_t launch_mt(const CUtensorMap& tm_p, const sc_weight* w, const uint16_t* bias, void* y, int64_t m,
+                      const int* shift, const long long* corr, long long* partials, uint32_t* counters, int grid,
+                      int* err, cudaStream_t stream) {
+  auto kernel = gemm_i8_skinny<kF32Out, MT>;
   static unsigned long long configured = 0;  // per template instance and device
-  if (cudaError_t e = set_smem_once(kernel, static_cast<int>(kSmemBytes), configured); e != cudaSuccess) return e;
+  if (cudaError_t e = set_smem_once(kernel, static_cast<int>(smem_bytes<MT>()), configured); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = smem_bytes<MT>();
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, tm_x, w->tmap_values_half, static_cast<const float*>(w->scales), bias, y,
-                            static_cast<int>(m), static_cast<int>(w->n), static_cast<int>(w->k_pad / BK),
-                            static_cast<int>(w->n_pad / BN), partials, counters, err);
+  return cudaLaunchKernelEx(&cfg, kernel, w->tmap_values_wide, tm_p, static_cast<const float*>(w->scales), bias, y,
+                            static_cast<int>(m), static_cast<int>(w->n), static_cast<int>((w->k_pad + BKU - 1) / BKU),
+                            static_cast<int>(w->n_pad / BN), shift, corr, partials, counters, err);
 }
 
-template <int kKind, bool kNaN, bool kF32Out>
-cudaError_t launch_kind(const CUtensorMap& tm_x, const sc_weight* w, const uint16_t* bias, void* y, int64_t m,
-                        float* partials, uint32_t* counters, int grid, int* err, cudaStream_t stream) {
-  if (m <= 16) return launch_mt<kKind, kNaN, kF32Out, 16>(tm_x, w, bias, y, m, partials, counters, grid, err, stream);
-  return launch_mt<kKind, kNaN, kF32Out, 32>(tm_x, w, bias, y, m, partials, counters, grid, err, stream);
-}
+}  // namespace skinny_i8
 
-}  // namespace skinny_sk
-
-// CTAs of the streamed skinny product for this weight (0 when it does not apply: fewer units than SMs'
-// worth of work, a share crossing more tiles than a CTA keeps partials for, or too many tiles to count).
-int skinny_sk_grid(const sc_weight* w, int sm_count) {
-  using namespace skinny_sk;
-  const int64_t k_tiles = w->k_pad / BK, n_tiles = w->n_pad / BN, units = k_tiles * n_tiles;
+// CTAs of the int8 skinny product for this weight and m (0 when it does not apply: not int8, m beyond 16
+// rows, K beyond the s32 accumulators' exact range, fewer units than two per SM, too many tiles to count).
+int skinny_i8_grid(const sc_weight* w, int64_t m, int sm_count) {
+  using namespace skinny_i8;
+  if (w->kind != SC_WEIGHT_INT8 || m > kSkinnyI8MaxRows || w->k_pad > 65536) return 0;
+  const int64_t k_tiles = (w->k_pad + BKU - 1) / BKU, n_tiles = w->n_pad / BN, units = k_tiles * n_tiles;
   if (n_tiles > kSkinnyCounterWords || units < 2 * static_cast<int64_t>(sm_count)) return 0;
-  const int64_t per = (units + sm_count - 1) / sm_count;
-  if ((per - 1) / k_tiles + 2 > kMaxSegments) return 0;
   return sm_count;
 }
 
-size_t skinny_sk_workspace_bytes(int grid) {
-  using namespace skinny_sk;
-  return static_cast<size_t>(grid) * kMaxSegments * BN * kMaxTokens * sizeof(float);
+// Workspace: the planes [3 MT][k_pad] int8, the rows' shifts and corrections, the CTAs' partial slots.
+size_t skinny_i8_workspace_bytes(const sc_weight* w, int64_t m, int grid) {
+  using namespace skinny_i8;
+  (void)m;
+  const size_t planes = (static_cast<size_t>(3 * kTokens) * w->k_pad + 255) / 256 * 256;
+  return planes + 1024 + static_cast<size_t>(grid) * kSlots * BN * kTokens * sizeof(long long);
 }
 
-cudaError_t launch_gemm_skinny_sk(const CUtensorMap& tmap_x, const sc_weight* w, const uint16_t* bias, void* y,
-                                  bool f32_out, int64_t m, float* partials, uint32_t* counters, int grid, int* err,
-                                  cudaStream_t stream) {
-  using namespace skinny_sk;
-  if (w->kind == SC_WEIGHT_INT8)
-    return f32_out ? launch_kind<1, false, true>(tmap_x, w, bias, y, m, partials, counters, grid, err, stream)
-                   : launch_kind<1, false, false>(tmap_x, w, bias, y, m, partials, counters, grid, err, stream);
-  if (w->has_nan_codes)
-    return f32_out ? launch_kind<2, true, true>(tmap_x, w, bias, y, m, partials, counters, grid, err, stream)
-                   : launch_kind<2, true, false>(tmap_x, w, bias, y, m, partials, counters, grid, err, stream);
-  return f32_out ? launch_kind<2, false, true>(tmap_x, w, bias, y, m, partials, counters, grid, err, stream)
-                 : launch_kind<2, false, false>(tmap_x, w, bias, y, m, partials, counters, grid, err, stream);
+cudaError_t launch_gemm_skinny_i8(sc_encode_tiled_fn encode, const uint16_t* x, const sc_weight* w,
+                                  const uint16_t* bias, void* y, bool f32_out, int64_t m, void* workspace,
+                                  uint32_t* counters, int grid, int* err, cudaStream_t stream) {
+  using namespace skinny_i8;
+  constexpr int mt = kTokens;
+  const size_t planes_bytes = (static_cast<size_t>(3 * mt) * w->k_pad + 255) / 256 * 256;
+  int8_t* planes = static_cast<int8_t*>(workspace);
+  int* shift = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + planes_bytes);
+  long long* corr = reinterpret_cast<long long*>(static_cast<uint8_t*>(workspace) + planes_bytes + 256);
+  long long* partials = reinterpret_cast<long long*>(static_cast<uint8_t*>(workspace) + planes_bytes + 1024);
+  // the planes as the MMA's B operand: rows of k_pad bytes, boxes of 128 bytes x 3 MT rows, swizzled
+  CUtensorMap tm_p;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w->k_pad), static_cast<cuuint64_t>(3 * mt)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w->k_pad)};
+  const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(3 * mt)};
+  const cuuint32_t estr[2] = {1, 1};
+  if (encode(&tm_p, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, planes, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+      CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(mt), 1, 1);
+    cfg.blockDim = dim3(kPlaneThreads, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaError_t e = cudaLaunchKernelEx(&cfg, x_planes, x, static_cast<int>(m), static_cast<int>(w->k),
+                                           static_cast<int>(w->k_pad), mt, planes, shift, corr);
+        e != cudaSuccess)
+      return e;
+  }
+  return f32_out ? launch_mt<true, kTokens>(tm_p, w, bias, y, m, shift, corr, partials, counters, grid, err, stream)
+                 : launch_mt<false, kTokens>(tm_p, w, bias, y, m, shift, corr, partials, counters, grid, err, stream);
 }
 
 }  // namespace sc

@@ -60,7 +60,7 @@ struct sc_ctx {
   // creation; every launch that uses them returns them to zero as its last CTA leaves.
   uint32_t* d_widen = nullptr;
   sc_counter_guard widen_guard;
-  // The streamed skinny product's tile counters (kSkinnyCounterWords), zeroed at creation; the last CTA of
+  // The int8 skinny product's tile counters (kSkinnyCounterWords), zeroed at creation; the last CTA of
   // each tile returns its counter to zero.
   uint32_t* d_skinny = nullptr;
   sc_counter_guard skinny_guard;
@@ -83,6 +83,8 @@ struct sc_weight {
   int device = -1;
   CUtensorMap tmap_values;    // 2D map over values: inner K (bytes), outer N rows; box 64 x 256
   CUtensorMap tmap_values_half;  // the same, box 64 x 128 (the half tile one CTA of a pair converts)
+  CUtensorMap tmap_values_wide;  // the same, box 128 x 128 with 128-byte swizzle (the int8 skinny product's
+                                 // MMA operand as stored; 16 KB a copy)
 };
 
 namespace sc {
@@ -203,15 +205,20 @@ cudaError_t launch_gemm_skinny(const CUtensorMap& tmap_x, const sc_weight* w, co
                                bool f32_out, int64_t m, int* err, int sm_count, cudaStream_t stream);
 // Rows above which sc_linear leaves the GEMV for the skinny tensor-core product.
 constexpr int64_t kSkinnyMinRows = 4;
-// The skinny product streamed in equal shares over one CTA per SM (sc_gemm_skinny_sk.cu): its grid for a
-// weight (0: the cluster kernel above serves it), its workspace (the tiles' fp32 partials), and the launch
-// (counters: the context's kSkinnyCounterWords tile counters, zero between launches).
+// The int8 skinny product on the integer tensor cores (sc_gemm_skinny_sk.cu): x written as three exact 8-bit
+// digit planes, the codes multiplied as stored, the work split in equal shares over one CTA per SM, for
+// 4 < m <= kSkinnyI8MaxRows (above that the planes' share of the operand traffic makes the cluster kernel
+// faster: on B200, 33.5 against 40.6 us a layer of config 4's chain at 24 and 32 rows).  Its grid for a
+// weight and m (0: the cluster kernel above serves it), its workspace (the planes, and the tiles' integer
+// partials) and the launch (counters: the context's kSkinnyCounterWords tile counters, zero between
+// launches).
 constexpr int kSkinnyCounterWords = 8192;
-int skinny_sk_grid(const sc_weight* w, int sm_count);
-size_t skinny_sk_workspace_bytes(int grid);
-cudaError_t launch_gemm_skinny_sk(const CUtensorMap& tmap_x, const sc_weight* w, const uint16_t* bias, void* y,
-                                  bool f32_out, int64_t m, float* partials, uint32_t* counters, int grid, int* err,
-                                  cudaStream_t stream);
+constexpr int64_t kSkinnyI8MaxRows = 16;
+int skinny_i8_grid(const sc_weight* w, int64_t m, int sm_count);
+size_t skinny_i8_workspace_bytes(const sc_weight* w, int64_t m, int grid);
+cudaError_t launch_gemm_skinny_i8(sc_encode_tiled_fn encode, const uint16_t* x, const sc_weight* w,
+                                  const uint16_t* bias, void* y, bool f32_out, int64_t m, void* workspace,
+                                  uint32_t* counters, int grid, int* err, cudaStream_t stream);
 
 // CTA count and workspace of the skinny product.
 int gemv_splits(const sc_weight* w, int64_t m, int sm_count);

@@ -404,6 +404,17 @@ __device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t adesc,
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, 8-bit integer operands, s32 accumulate (kind::i8, one CTA).
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                                uint32_t accumulate) {
   asm volatile(
@@ -447,6 +458,15 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t start) {
 // Instruction descriptor: bf16 x bf16 -> fp32, both operands K-major, tile M x N.
 // kind::i8: D s32, A and B signed 8-bit, both K-major, no saturation (the int32 sums wrap, as the
 // exact sums of int8 products do not for K below 2^17).
+// kind::i8 with A unsigned 8-bit (the arena's biased int8 codes, u = q + 128) and B signed 8-bit.
+__host__ __device__ constexpr uint32_t umma_idesc_u8s8(int m, int n) {
+  return (2u << 4)                                  // D format: s32
+         | (0u << 7)                                // A format: unsigned 8-bit
+         | (1u << 10)                               // B format: signed 8-bit
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
 __host__ __device__ constexpr uint32_t umma_idesc_s8(int m, int n) {
   return (2u << 4)                                  // D format: s32
          | (1u << 7)                                // A format: signed 8-bit

@@ -252,30 +252,25 @@ def test_skinny_tensor_core_product_agrees_with_gemv(ctx, kind, m, nan):
     w.close()
 
 
-@pytest.mark.parametrize("kind,m,k,n", [(abi.WEIGHT_INT8, 16, 4096, 12288), (abi.WEIGHT_INT8, 32, 12288, 4096),
-                                         (abi.WEIGHT_E4M3, 7, 1024, 4000), (abi.WEIGHT_INT8, 9, 256, 38400)])
-def test_streamed_skinny_product_matches_the_oracle_and_repeats(ctx, kind, m, k, n):
-    """With its workspace, 4 < m <= 32 streams the weight in equal shares over one CTA per SM (a share
-    crosses tiles: the last of K = 256's shares span three); the tiles' partials meet in K order.  fp32
-    output within the oracle's bar, the same bits on a second call, and within the bar of the cluster
-    kernel that runs without the workspace."""
+@pytest.mark.parametrize("m,k,n", [(16, 4096, 12288), (12, 12288, 4096), (7, 2048, 8000), (9, 512, 38400), (13, 3000, 3200)])
+def test_int8_skinny_product_matches_the_oracle_and_repeats(ctx, m, k, n):
+    """With its workspace, an int8 product of 4 < m <= 16 rows runs on the integer tensor cores: x as three
+    exact 8-bit digit planes, the codes as stored, the weight split in equal shares over one CTA per SM (with
+    K = 512 a tile is two units and a share four or five: partials meet through the fix-up).  fp32 output
+    within the oracle's bar (the integer sum is exact where the oracle's fp32 sum rounds), the same bits on a
+    second call, within the bar of the cluster kernel that runs without the workspace, and bf16 output
+    within the GEMM bar of the oracle's bf16 result."""
     g = np.random.default_rng(m * k + n)
-    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
-    if kind == abi.WEIGHT_INT8:
-        q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
-    else:
-        q = configs.to_e4m3_codes(g.standard_normal((k, n), dtype=np.float32) * 4)
-        q[(q & 0x7F) == 0x7F] ^= 1
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32) * 2.0 ** g.integers(-3, 2, (m, 1)))
+    x[0, : k // 3] = 0                                            # a stretch of zeros
+    x[1, 5] = configs.to_bf16_bits(np.array([1e-30], np.float32))[0]  # far below the row's largest
+    q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
     s = (np.abs(g.standard_normal(n)) * 0.01 / 127 + 1e-6).astype(np.float32)
     b = configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.01)
-    w = QuantizedWeight(ctx, q, kind, s)
-    assert w.workspace_bytes(m) > 0, "the streamed route applies"
+    w = QuantizedWeight(ctx, q, abi.WEIGHT_INT8, s)
+    assert w.workspace_bytes(m) > 0, "the integer route applies"
     xd, bd = bf16_dev(x), bf16_dev(b)
-    if kind == abi.WEIGHT_INT8:
-        c_ref, y_ref = oracle.linear_int8(x, q.view(np.int8), s, b)
-    else:
-        wf = oracle.dequantize(q, oracle.E4M3, s, oracle.SCALE_F32, oracle.LAYOUT_COLUMNS, n).reshape(k, n)
-        c_ref, y_ref = oracle.linear_widened(x, wf, b)
+    c_ref, y_ref = oracle.linear_int8(x, q.view(np.int8), s, b)
     first = host(linear_ex(ctx, w, xd, m, bd, True))
     again = host(linear_ex(ctx, w, xd, m, bd, True))
     cluster = host(linear_ex(ctx, w, xd, m, bd, True, workspace=False))
@@ -283,7 +278,46 @@ def test_streamed_skinny_product_matches_the_oracle_and_repeats(ctx, kind, m, k,
     assert np.array_equal(first.view(np.uint32), again.view(np.uint32)), "the same bits on a second call"
     assert rel_l2(cluster, first) <= REL_L2_F32
     y16 = f32_of_bf16(bf16_host(linear_ex(ctx, w, xd, m, bd, False)))
-    assert rel_l2(y16, f32_of_bf16(y_ref)) <= REL_L2_BF16
+    rf = f32_of_bf16(y_ref)
+    assert rel_l2(y16, rf) <= REL_L2_BF16 and float(np.max(np.abs(y16.astype(np.float64) - rf))) <= MAX_ABS_BF16
+    w.close()
+
+
+def test_int8_products_of_17_to_32_rows_take_no_workspace(ctx):
+    """Above 16 rows the int8 skinny product is the cluster kernel (no workspace): the reported size is 0
+    and the product still meets the oracle's bar."""
+    k, n = 4096, 4096   # 512 units of 128 x 256: at least two per SM, so 16 rows take the integer route
+    g = np.random.default_rng(17)
+    q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+    s = (np.abs(g.standard_normal(n)) * 0.01 / 127 + 1e-6).astype(np.float32)
+    w = QuantizedWeight(ctx, q, abi.WEIGHT_INT8, s)
+    assert w.workspace_bytes(16) > 0
+    for m in (17, 24, 32):
+        assert w.workspace_bytes(m) == 0, m
+    w.close()
+    x = configs.to_bf16_bits(g.standard_normal((20, k), dtype=np.float32))
+    check_against_oracle(ctx, abi.WEIGHT_INT8, x, q, s, None, "int8 m=20")
+
+
+def test_int8_skinny_product_with_zero_and_nonfinite_rows(ctx):
+    """A row of x that is all zeros gives the bias; a row holding an infinity gives NaN (its products meet
+    weights of both signs); the other rows are unaffected."""
+    m, k, n = 8, 2048, 8192
+    g = np.random.default_rng(5)
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    x[2] = 0
+    x[5, 77] = 0x7F80                                            # +inf
+    q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+    s = (np.abs(g.standard_normal(n)) * 0.01 / 127 + 1e-6).astype(np.float32)
+    b = configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.01)
+    w = QuantizedWeight(ctx, q, abi.WEIGHT_INT8, s)
+    assert w.workspace_bytes(m) > 0
+    y = host(linear_ex(ctx, w, bf16_dev(x), m, bf16_dev(b), True))
+    assert np.array_equal(y[2], f32_of_bf16(b))
+    assert np.isnan(y[5]).all()
+    keep = [r for r in range(m) if r not in (2, 5)]
+    c_ref, _ = oracle.linear_int8(x[keep], q.view(np.int8), s, b)
+    assert rel_l2(y[keep], c_ref) <= REL_L2_F32
     w.close()
 
 
