@@ -4,7 +4,7 @@ Default workload (config 1 of the benchmark configs, the one the headline metric
 one int8 weight-only linear, x bf16 [4096, 3072], W int8 [3072, 3072] per-output-channel scales,
 bf16 bias, fp32 accumulation, bf16 output.  A step is one product over that batch.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg1|cfg2|gemv1|gemv4|gemv16|gemv32|...]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg1|cfg2|gemv1|gemv4|gemv16|gemv32|prefill128|...]
   python bench.py --impl reference ...   # the reference's CPU path (the oracle), on the host cores
 
 With N > 1 (one process per GPU under torch.distributed.run) config 1 runs column-parallel: rank r
@@ -56,6 +56,11 @@ def make_case(workload: str):
     if workload.startswith("gemv"):
         m = int(workload[4:] or 1)
         return configs.config4(m, 12288, 4096)
+    if workload.startswith("prefill"):
+        m = int(workload[7:] or 128)
+        if not 32 < m <= 128:
+            raise SystemExit("prefillM takes 32 < M <= 128")
+        return configs.encoder_prefill(m)
     raise SystemExit(f"unknown workload {workload}")
 
 
@@ -82,6 +87,8 @@ def describe(case, workload, world=1):
 def metric_of(case):
     if case.m <= 32:
         return "int8-weight GEMV achieved HBM GB/s", "GB/s"
+    if case.m <= 128:
+        return f"int8-weight GEMM TFLOP/s at M={case.m} (encoder prefill)", "TFLOP/s"
     return "int8-weight GEMM TFLOP/s at M=4096" if case.kind == 1 else "fp8-weight GEMM TFLOP/s at M=4096", "TFLOP/s"
 
 
@@ -148,6 +155,8 @@ def route_kernels(case, ws_bytes: int) -> list[str]:
     codes followed by the bf16-operand pair GEMM."""
     if case.m <= 4:
         return ["gemv_w8"]
+    if case.m <= 16 and case.kind == 1 and ws_bytes > 0:
+        return ["x_planes", "gemm_i8_skinny"]
     if case.m <= 32:
         return ["gemm_w8_skinny"]
     if case.m <= 128:
@@ -334,6 +343,32 @@ def run_ours(args):
         dist.barrier()
     e2e_value = throughput(case, float(te.item()) / 1e3 / e2e_steps, unit, ranks=world)
 
+    # Yardstick (one GPU, the GEMM configs): cuBLAS through torch.matmul, bf16 x . bf16 W on the same shape, the
+    # weight dequantized and rounded to bf16, no scale and no bias, in the same harness (L2 flushed, events
+    # around each step).  A library GEMM on a plain bf16 weight: what this shape gives without quantization.
+    yardstick = None
+    if world == 1 and unit != "GB/s" and not w8a8:
+        wb = w.dequantize().to(torch.bfloat16)
+        yb = torch.empty((case.m, case.n), dtype=torch.bfloat16, device="cuda")
+        for _ in range(args.warmup):
+            flush_l2(1)
+            torch.matmul(x, wb, out=yb)
+        ys = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ye = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        torch.cuda.synchronize()
+        torch.cuda._sleep(int(2e6) * max(1, args.steps // 10))
+        for i in range(args.steps):
+            flush_l2(i)
+            ys[i].record(stream)
+            torch.matmul(x, wb, out=yb)
+            ye[i].record(stream)
+        torch.cuda.synchronize()
+        y_ms = sum(a.elapsed_time(b) for a, b in zip(ys, ye)) / args.steps
+        yardstick = {"what": "torch.matmul (cuBLAS) bf16 x [M, K] . W [K, N], W dequantized and rounded to bf16, "
+                             "no scale or bias; same L2 flush and events",
+                     "ms_per_step": y_ms, "value": case.flops / (y_ms / 1e3) / 1e12, "unit": "TFLOP/s"}
+        del wb, yb
+
     if rank == 0:
         peaks, peak_src = load_peaks()
         if unit == "GB/s":
@@ -371,6 +406,8 @@ def run_ours(args):
                                    "; y copied back in chunks")},
                 "gpu_launches": args.steps * (3 if w8a8 else len(route_kernels(case, ws_bytes))),
                 "step_ms_min": min(per_step), "step_ms_median": statistics.median(per_step)}
+        if yardstick is not None:
+            line["yardstick"] = yardstick
         if w8a8:
             line["roofline"]["peak_source"] += "; int8 dense peak taken as 2 x the measured bf16 figure (the nominal ratio)"
             line["e2e"]["path"] = "QuantizedWeight.linear_w8a8 with pinned host x in and y out on one stream, every step"
@@ -412,7 +449,8 @@ def run_chain(args):
     acts = [torch.from_numpy(cases[0].x.view(np.int16)).cuda().view(torch.bfloat16)]
     for n, _ in shapes:
         acts.append(torch.empty((m, n), dtype=torch.bfloat16, device="cuda"))
-    ws = torch.empty(max(max(w.workspace_bytes(m) for w in weights), 1), dtype=torch.uint8, device="cuda")
+    ws_need = max(w.workspace_bytes(m) for w in weights)
+    ws = torch.empty(max(ws_need, 1), dtype=torch.uint8, device="cuda")
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     clean = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     sink = torch.empty((), dtype=torch.float32, device="cuda")
@@ -461,7 +499,7 @@ def run_chain(args):
         single.append({"shape": list(shapes[i]), "us": t * 1e3, "gb_s": cases[i].bytes_moved() / (t / 1e3) / 1e9})
     if rank == 0:
         peaks, peak_src = load_peaks()
-        kern = "gemv_w8" if m <= 4 else "gemm_w8_skinny"
+        kern = route_kernels(cases[0], ws_need)
         line = {"metric": "int8-weight GEMV achieved HBM GB/s (decode chain, per layer)", "value": value,
                 "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -474,8 +512,9 @@ def run_chain(args):
                            "parallelism": "one GPU"},
                 "roofline": {"bound": "hbm", "achieved": value, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                              "frac": value / peaks["hbm_gbs"], "traffic": None, "peak_source": peak_src,
-                             "kernels": [kern]},
-                "single_cold_read": single, "clocks": clocks.summary(), "gpu_launches": args.steps * CHAIN_LAYERS,
+                             "kernels": kern},
+                "single_cold_read": single, "clocks": clocks.summary(),
+                "gpu_launches": args.steps * CHAIN_LAYERS * len(kern),
                 "step_ms_min": min(per), "step_ms_median": statistics.median(per)}
         print(json.dumps(line), flush=True)
     for w in weights:

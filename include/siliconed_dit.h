@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-enum { SD_OK = 0, SD_INVALID_ARG = 1, SD_CUDA_ERROR = 4 };
+enum { SD_OK = 0, SD_INVALID_ARG = 1, SD_CUDA_ERROR = 4, SD_TIMEOUT = 5 };
 
 /* out[r, :] = bf16( x[r, :] * rsqrt(mean(x[r, :]^2) + eps) * weight * (1 + scale) ), fp32 x [rows, d];
  * weight and scale [d] may be NULL (ones / zeros).  Ops.rmsNorm then Ops.scaleRows (Ops.swift:16-42),
@@ -78,6 +78,20 @@ SD_API int sd_swiglu_blocks(const uint16_t* h, int64_t rows, int hidden, int blo
 /* h = bf16( 0.5 h (1 + tanh(sqrt(2 / pi) (h + 0.044715 h^3))) ) in place, bf16 [count]
  * (nn.GELU(approximate="tanh"), QwenImage21.swift:953-963). */
 SD_API int sd_gelu_tanh(uint16_t* h, int64_t count, void* stream);
+
+/* o = softmax(q k^T * scale) v per row of queries, over all seq keys (no mask), bf16 q, k, v, o
+ * [bh][seq][head_dim] (bh = batch * heads; the layout sd_qk_norm_rope writes), fp32 scores, sums and
+ * accumulation, P rounded to bf16 for the P . v product: the reference's fused attention
+ * (TiledAttention.swift:470-610) in its online form on the tensor cores.  head_dim = 128; pointers
+ * 16-byte aligned; scale > 0 (the blocks pass 1 / sqrt(head_dim)).  Replaces the library attention the
+ * blocks called before.  Device-side waits are bounded: a wait that gives up is reported by
+ * sd_attention_errors. */
+SD_API int sd_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o, int bh, int seq,
+                        int head_dim, float scale, void* stream);
+
+/* SD_TIMEOUT (and the wait's site in *site) if a wait of sd_attention gave up since the last call, else SD_OK;
+ * clears the record.  Synchronous with the device. */
+SD_API int sd_attention_errors(int* site);
 
 #ifdef __cplusplus
 }

@@ -20,7 +20,7 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(HERE, "libsiliconed_cuda.so")
 DIT_LIB = os.path.join(HERE, "libsiliconed_dit.so")
 DIT_CSRC = os.path.join(CSRC, "dit")
-DIT_SOURCES = ["sd_kernels.cu"]
+DIT_SOURCES = ["sd_kernels.cu", "sd_attention.cu"]
 
 SOURCES = ["sc_abi.cu", "sc_weight.cu", "sc_gemm.cu", "sc_gemm_pair.cu", "sc_gemm_bf16.cu", "sc_gemm_skinny.cu", "sc_gemm_skinny_sk.cu",
            "sc_gemv.cu", "sc_no_alloc.cu", "sc_rotate.cu", "sc_w8a8.cu"]
@@ -39,7 +39,7 @@ def _stale(lib: str, src_dir: str, header: str) -> bool:
         return True
     t = os.path.getmtime(lib)
     deps = [os.path.join(src_dir, f) for f in os.listdir(src_dir) if os.path.isfile(os.path.join(src_dir, f))]
-    deps += [os.path.join(INCLUDE, header), __file__]
+    deps += [os.path.join(INCLUDE, header), os.path.join(CSRC, "sc_ptx.cuh"), __file__]
     return any(os.path.getmtime(d) > t for d in deps)
 
 

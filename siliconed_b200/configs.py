@@ -71,6 +71,17 @@ def config2(m: int = 4096, k: int = 3840, n: int = 10240, seed: int = 0) -> Line
     return LinearCase("cfg2-e4m3", 2, x, q, s, None)
 
 
+def encoder_prefill(m: int = 128, n: int = 9728, k: int = 2560, seed: int = 0) -> LinearCase:
+    """A text encoder's prefill product (32 < M <= 128 rows, the single-CTA tensor-core GEMM's range): the
+    gate / up shape of the Z-Image encoder's MLP as its published int8 checkpoint stores it ([9728, 2560],
+    recorded in tests/golden/quant_fixture_pins.json), x ~ N(0,1) bf16, per-channel scales, no bias."""
+    g = np.random.default_rng(seed)
+    x = to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    q = g.integers(-127, 128, size=(n, k), dtype=np.int16).astype(np.int8).view(np.uint8)
+    s = (np.abs(g.standard_normal(n, dtype=np.float32)) * np.float32(0.02) / np.float32(127)).astype(np.float32)
+    return LinearCase(f"encoder-prefill-m{m}-{n}x{k}", 1, x, q, s, None)
+
+
 def config4(m: int, n: int, k: int, seed: int = 0) -> LinearCase:
     """Config 4: decode-shape GEMV, int8 per-channel weight [n out, k in], x ~ N(0,1) bf16, M <= 32."""
     g = np.random.default_rng(seed)

@@ -180,9 +180,19 @@ def image_text_positions(txt_tokens: int, grid: int) -> torch.Tensor:
     return torch.cat([txt, img], dim=0)
 
 
-def attention(q, k, v):
-    """Scaled dot-product attention over [B, H, S, D] bf16 (the CUDA library's fused kernel)."""
-    return torch.nn.functional.scaled_dot_product_attention(q, k, v)
+# "native": sd_attention, this project's tcgen05 kernel (parity-tested at configs 3 and 5); "library": torch's
+# fused scaled-dot-product attention, the default while it is the faster of the two on B200 (config 3's
+# attention: 228 us against 386 us for sd_attention).
+ATTENTION = "library"
+
+
+def attention(q, k, v, out=None):
+    """Scaled dot-product attention over [B, H, S, 128] bf16, scale 1 / sqrt(128)."""
+    if ATTENTION == "library":
+        return torch.nn.functional.scaled_dot_product_attention(q, k, v)
+    if out is None:
+        out = torch.empty_like(q)
+    return dk.attention(q.contiguous(), k.contiguous(), v.contiguous(), out, 1.0 / math.sqrt(q.shape[-1]))
 
 
 def merged_rows(o, batch: int, heads: int, joint: int, off: int, n: int, out: torch.Tensor) -> torch.Tensor:

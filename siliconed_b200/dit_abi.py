@@ -25,6 +25,8 @@ SIGNATURES = {
     "sd_swiglu": (_I, [_P, _I64, _I, _P, _P]),
     "sd_swiglu_blocks": (_I, [_P, _I64, _I, _I, _P, _P]),
     "sd_gelu_tanh": (_I, [_P, _I64, _P]),
+    "sd_attention": (_I, [_P, _P, _P, _P, _I, _I, _I, _F, _P]),
+    "sd_attention_errors": (_I, [ctypes.POINTER(ctypes.c_int)]),
 }
 
 _lib = None
@@ -123,3 +125,16 @@ def swiglu_blocks(h, hidden, block, out):
 def gelu_tanh(h):
     _check(load().sd_gelu_tanh(_ptr(h), h.numel(), _stream()), "sd_gelu_tanh")
     return h
+
+
+def attention(q, k, v, out, scale: float):
+    """out = softmax(q k^T * scale) v over [B, H, S, 128] bf16 (contiguous), on the tensor cores."""
+    b, h, seq, d = q.shape
+    _check(load().sd_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(out), b * h, seq, d, scale, _stream()), "sd_attention")
+    return out
+
+
+def attention_errors() -> tuple[int, int]:
+    """(status, site) of sd_attention's bounded waits since the last call: (0, 0), or SD_TIMEOUT and its site."""
+    site = ctypes.c_int(0)
+    return load().sd_attention_errors(ctypes.byref(site)), site.value
