@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -796,6 +797,65 @@ def run_colpar(args):
 
 
 DIT_WORKLOADS = ("cfg3", "cfg5")
+ATTN_SHAPES = {"attn3": (1, 30, 4608), "attn5": (8, 24, 4352)}  # [batch, heads, joint tokens], head_dim 128
+
+
+def run_attention(args):
+    """attn3 / attn5: the attention of config 3 (1 x 30 heads x 4608 tokens) or config 5 (8 images x 24 heads x
+    4352 joint tokens) alone, sd_attention on bf16 q, k, v [B, H, S, 128] (seeded N(0, 1)), with torch's fused
+    SDPA on the same inputs timed beside it as the yardstick.  value: 4 B H S^2 128 FLOP over the device time of
+    one call; the inputs (141 MB / 580 MB) exceed the L2, and the L2 is flushed before every step anyway."""
+    import torch
+    from siliconed_b200 import dit_abi
+
+    b, h, s = ATTN_SHAPES[args.workload]
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q, k, v = (torch.randn(b, h, s, 128, generator=g, device="cuda").to(torch.bfloat16) for _ in range(3))
+    o = torch.empty_like(q)
+    flops = 4.0 * b * h * s * s * 128
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            flush.fill_(1)
+            fn()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        torch.cuda._sleep(int(2e6))
+        for i, (a, e) in enumerate(ev):
+            flush.fill_(i & 0xFF)
+            a.record(stream)
+            fn()
+            e.record(stream)
+        torch.cuda.synchronize()
+        per = [a.elapsed_time(e) for a, e in ev]
+        return sum(per) / len(per), per
+
+    with ClockSampler(0) as clocks:
+        ms, per = timed(lambda: dit_abi.attention(q, k, v, o, 1.0 / math.sqrt(128)))
+    status = dit_abi.attention_errors()
+    if status != (0, 0):
+        raise SystemExit(f"sd_attention: a bounded wait gave up {status}")
+    ms_lib, _ = timed(lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v))
+    peaks, peak_src = load_peaks()
+    value = flops / (ms / 1e3) / 1e12
+    line = {"metric": "attention TFLOP/s (head_dim 128, bf16)", "value": value, "unit": "TFLOP/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{args.workload}: softmax(q k^T / sqrt(128)) v, q, k, v, o bf16 [{b}, {h}, {s}, 128]",
+                       "batch": b, "heads": h, "seq": s, "l2": "flushed before every timed step",
+                       "parallelism": "one GPU"},
+            "roofline": {"bound": "tensor", "achieved": value, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": value / peaks["bf16_tflops"], "traffic": None,
+                         "peak_source": f"{peak_src} (burst figure)", "kernels": ["attention_fwd"]},
+            "yardstick": {"what": "torch.nn.functional.scaled_dot_product_attention on the same bf16 inputs",
+                          "ms_per_step": ms_lib, "value": flops / (ms_lib / 1e3) / 1e12, "unit": "TFLOP/s"},
+            "clocks": clocks.summary(), "gpu_launches": args.steps,
+            "step_ms_min": min(per), "step_ms_median": statistics.median(per)}
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def dit_cpu_seconds(shapes, rows_full: int, rows_sample: int = 256):
@@ -1029,6 +1089,12 @@ def main():
         return run_scale(args)
     if args.workload.startswith("chain") and args.impl == "ours":
         return run_chain(args)
+    if args.workload in ATTN_SHAPES:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the attention workloads have no CPU reference arm "
+                              "(the yardstick on the ours line is the library's GPU attention)"}), flush=True)
+            return 0
+        return run_attention(args)
     if args.workload in DIT_WORKLOADS:
         if args.impl == "reference":
             rank = int(os.environ.get("RANK", "0"))

@@ -10,20 +10,25 @@
 // and may reach 256, which fp32 sums and bf16 P carry without loss of relative precision.  The result is the same
 // quotient; fewer O passes.
 //
-// One CTA per 128 query rows of one head (the grid's tiles of one head consecutive, so the head's k and v stay in
+// One CTA per 128 query rows of one head (the grid's CTAs of one head consecutive, so the head's k and v stay in
 // L2 while they are read).  Roles:
-// - warp 0, one thread: TMA.  q's tile once ([128 rows][128 dims] as two 128-byte-swizzled boxes of 64 dims), then
-//   k and v tiles of 128 keys through rings of two 32 KB stages each.  Coordinates past seq read zeros.
-// - warp 1, one thread: the MMAs.  S_j = q k_j^T (tcgen05.mma kind::f16, M 128, N 128, both operands K-major from
-//   shared memory) into one of two TMEM buffers of 128 fp32 columns, two tiles ahead of the softmax; then
-//   O += P_j v_j with P_j read from TMEM (the A operand, bf16 pairs in the S buffer's first 64 columns) and v_j
-//   from shared memory as an MN-major B operand (its 128-byte rows are keys, 64 dims each: LBO = the 16 KB between
-//   the two dim halves, SBO = 1 KB between 8-key groups).  O lives in TMEM for the CTA's whole run.
-// - warps 4-7: the softmax, one query row per thread (TMEM lane = row).  Each reads its row of S_j (128 fp32),
-//   masks keys past seq, takes the maximum, forms exp2(s c - m) (c = scale log2 e; ex2.approx), adds them to l,
-//   packs them to bf16 pairs and writes them back into the buffer for the MMA.  Before writing P_j it waits for
-//   P_{j-1} v_{j-1} to finish, so that a rescale of O (a warp reads, scales and writes its rows' O) sees it whole.
-//   At the end: O / l, rounded to bf16, stored row by row.
+// - warp 4: TMA.  Lane 0 loads the q tile once ([128 rows][128 dims] as two 128-byte-swizzled boxes of 64 dims)
+//   and the k tiles of 128 keys through a ring of three 32 KB stages; lane 1 the v tiles through a ring of two (v
+//   is needed later than k).  Coordinates past seq read zeros.
+// - warp 5, one thread: the MMAs.  S_t = q k_t^T (tcgen05.mma kind::f16, M 128, N 128, both operands K-major from
+//   shared memory) into one of three TMEM buffers of 128 fp32 columns, three key tiles ahead of the softmax (with
+//   two, S_{t+1} could only start once P_{t-1} v had read its buffer, which chained every softmax to the MMAs of
+//   the tile before); then O += P_t v_t with P_t read from TMEM (the A operand, bf16 pairs in the S buffer's first
+//   64 columns) and v_t from shared memory as an MN-major B operand (its 128-byte rows are keys, 64 dims each:
+//   LBO = the 16 KB between the two dim halves, SBO = 1 KB between 8-key groups).  TMEM: S_0, S_1, S_2, O.
+// - warps 0-3: the softmax, one query row per thread (TMEM lane = row).  Each reads its row of S 32 columns at a
+//   time (the next load in flight while the last is used) and forms exp2(s c - m) with the row's running maximum m
+//   (c = scale log2 e; ex2.approx), their sum and their bf16 pairs.  The maximum itself is only taken when the
+//   tile's sum shows it moved far (the first tile; a sum above 2^32): then the tile is redone with the new maximum
+//   and O rescaled.  Until then exponentials above 1 are kept (fp32 sums and bf16 P carry them without loss of
+//   relative precision) and the result is the same quotient.  P goes back over the columns already read; before
+//   handing it over the warp waits for P_{t-1} v, so that a rescale of O sees it whole.  At the end: O / l,
+//   rounded to bf16, stored row by row.
 // Every wait is bounded (2 s): on expiry the kernel records SD_TIMEOUT's site in a device word, raises the CTA's
 // abort flag, drains and frees TMEM.  No load uses cluster multicast.
 #include <cuda.h>
@@ -43,29 +48,30 @@ using namespace sc;
 constexpr int kHeadDim = 128;
 constexpr int BQ = 128;                         // query rows a CTA
 constexpr int BK = 128;                         // keys a tile
-constexpr int kKV = 2;                          // ring stages for k and for v
+constexpr int kK = 3, kV = 2;                   // ring stages for k and for v
 constexpr int kTileBytes = BK * kHeadDim * 2;   // 32 KB
 constexpr int kBoxBytes = kTileBytes / 2;       // [128 rows][64 dims], 16 KB
-constexpr int kThreads = 256;
-constexpr int kSoftWarp0 = 4;                   // warps 4-7: TMEM lanes 0-127
+constexpr int kThreads = 192;                   // warps 0-3 softmax, 4 TMA, 5 MMA
+constexpr int kTmaWarp = 4, kMmaWarp = 5;
+constexpr int kSB = 3;                          // S / P buffers in TMEM
+constexpr float kMovedSum = 4294967296.0f;      // 2^32: a tile's sum above it means the maximum moved
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;                 // O: 128 fp32 columns (S / P buffers: columns 0 and 128)
-constexpr float kLazyLog2 = 8.0f;               // a row's maximum moves when exceeded by more than 2^8
 
-__device__ __forceinline__ uint32_t col_s(int j) { return (j & 1) ? 128u : 0u; }
+__device__ __forceinline__ uint32_t col_s(int t) { return static_cast<uint32_t>(t % kSB) * 128u; }  // S_t; P_t: first 64
+constexpr uint32_t kColO = 384;                                                                    // O: 128 columns
 
 enum : int { kSiteLoadEmpty = 21, kSiteScores = 22, kSiteProbs = 23, kSiteValues = 24, kSiteQuery = 25, kSiteOut = 26 };
 
 struct __align__(1024) Smem {
   uint8_t q[kTileBytes];
-  uint8_t k[kKV][kTileBytes];
-  uint8_t v[kKV][kTileBytes];
+  uint8_t k[kK][kTileBytes];
+  uint8_t v[kV][kTileBytes];
   uint64_t q_full;
-  uint64_t k_full[kKV], k_empty[kKV];
-  uint64_t v_full[kKV], v_empty[kKV];
-  uint64_t s_full[2];  // S_j complete in buffer j % 2 (MMA -> softmax)
-  uint64_t p_full[2];  // P_j written to buffer j % 2, S_j read (softmax -> MMA; one arrival per softmax warp)
-  uint64_t o_done;     // P_j v_j complete (MMA -> softmax), once per tile
+  uint64_t k_full[kK], k_empty[kK];
+  uint64_t v_full[kV], v_empty[kV];
+  uint64_t s_full[kSB];  // S_t complete in buffer t % 3 (MMA -> softmax)
+  uint64_t p_full[kSB];  // P_t written to buffer t % 3, S_t read (softmax -> MMA; one arrival per softmax warp)
+  uint64_t o_done;       // P_t v_t complete (MMA -> softmax), once per key tile
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -133,11 +139,83 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// One lane-0 wait broadcast to the warp (tcgen05.ld / st are warp-collective, so the warp moves together).
+// One lane-0 wait broadcast to the warp (tcgen05.ld / st are warp-collective, so the warp moves together).  The
+// handoffs between the softmax and the MMA thread are the kernel's critical path, so they poll with the
+// non-suspending probe: a suspending wait was seen to notice a completed phase 300-600 cycles late.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int site) {
   int got = 0;
-  if ((threadIdx.x & 31) == 0) got = mbar_wait(bar, parity, abort, err, site) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) got = mbar_poll(bar, parity, abort, err, site) ? 1 : 0;
   return __shfl_sync(0xFFFFFFFFu, got, 0) != 0;
+}
+
+// exp2(s c - m) over this row of a tile of S (keys at or past `valid` left out when kMasked), packed to bf16 pairs
+// in p (keys 2k, 2k + 1 in p[k]), and their fp32 sum; 32 columns at a time, the next load in flight.
+template <bool kMasked>
+__device__ __forceinline__ float row_exps(uint32_t sb, int valid, float c_log2, float m, uint32_t (&p)[BK / 2]) {
+  float sum4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  uint32_t r[2][32];
+  tmem_ld_32(sb, r[0]);
+#pragma unroll
+  for (int c = 0; c < BK / 32; ++c) {
+    tmem_wait_ld();
+    if (c + 1 < BK / 32) tmem_ld_32(sb + (c + 1) * 32, r[(c + 1) & 1]);
+    const uint32_t* x = r[c & 1];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      float s0 = __uint_as_float(x[2 * k]), s1 = __uint_as_float(x[2 * k + 1]);
+      if (kMasked) {
+        if (c * 32 + 2 * k >= valid) s0 = -INFINITY;
+        if (c * 32 + 2 * k + 1 >= valid) s1 = -INFINITY;
+      }
+      const float e0 = ex2(fmaf(s0, c_log2, -m));
+      const float e1 = ex2(fmaf(s1, c_log2, -m));
+      sum4[k & 3] += e0 + e1;
+      p[c * 16 + k] = pack_bf16x2(e0, e1);
+    }
+  }
+  return (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+}
+
+// The row's maximum of s over a tile (kMasked: the keys inside the sequence), times c.
+template <bool kMasked>
+__device__ __forceinline__ float row_max(uint32_t sb, int valid, float c_log2) {
+  float mx8[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < BK / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32(sb + c * 32, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      if (!kMasked || c * 32 + k < valid) mx8[k & 7] = fmaxf(mx8[k & 7], __uint_as_float(r[k]));
+  }
+  return c_log2 * fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])), fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+}
+
+// One tile of this row: P in p, its sum, the running maximum m and the factor alpha that l and O take.
+template <bool kMasked>
+__device__ __forceinline__ float softmax_tile(uint32_t sb, int valid, float c_log2, bool first, float& m, float& alpha,
+                                              uint32_t (&p)[BK / 2]) {
+  alpha = 1.0f;
+  if (first) {
+    m = row_max<kMasked>(sb, valid, c_log2);
+    return row_exps<kMasked>(sb, valid, c_log2, m, p);
+  }
+  float sum = row_exps<kMasked>(sb, valid, c_log2, m, p);
+  const bool moved = !(sum <= kMovedSum);  // (a NaN sum takes the slow path too)
+  if (__any_sync(0xFFFFFFFFu, moved)) {  // rare: S is still in TMEM, P not yet written back
+    // one call for the whole warp: tcgen05.ld is warp-collective (.sync.aligned), so every lane must reach the
+    // same instruction; the lanes whose maximum did not move keep theirs
+    const float mt = row_max<kMasked>(sb, valid, c_log2);
+    if (moved && mt > m) {
+      alpha = ex2(m - mt);
+      m = mt;
+    }
+    sum = row_exps<kMasked>(sb, valid, c_log2, m, p);
+  }
+  return sum;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -153,13 +231,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&s.q_full, 1);
-    for (int i = 0; i < kKV; ++i) {
+    for (int i = 0; i < kK; ++i) {
       mbar_init(&s.k_full[i], 1);
       mbar_init(&s.k_empty[i], 1);
+    }
+    for (int i = 0; i < kV; ++i) {
       mbar_init(&s.v_full[i], 1);
       mbar_init(&s.v_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kSB; ++i) {
       mbar_init(&s.s_full[i], 1);
       mbar_init(&s.p_full[i], 4);
     }
@@ -171,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&s.tmem_base, kTmemCols);
     tmem_relinquish();
   }
@@ -180,46 +260,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&s.q_full, kTileBytes);
-      tma_load_3d(s.q, &tm_q, &s.q_full, 0, q0, bh);
-      tma_load_3d(s.q + kBoxBytes, &tm_q, &s.q_full, 64, q0, bh);
+  if (warp == kTmaWarp) {
+    // ---------------- TMA producers: q and k (lane 0), v (lane 1) ----------------
+    if (lane < 2) {
+      const bool keys = lane == 0;
+      const int stages = keys ? kK : kV;
+      uint64_t* full = keys ? s.k_full : s.v_full;
+      uint64_t* empty = keys ? s.k_empty : s.v_empty;
+      const CUtensorMap* map = keys ? &tm_k : &tm_v;
+      if (keys) {
+        mbar_arrive_expect_tx(&s.q_full, kTileBytes);
+        tma_load_3d(s.q, &tm_q, &s.q_full, 0, q0, bh);
+        tma_load_3d(s.q + kBoxBytes, &tm_q, &s.q_full, 64, q0, bh);
+      }
       uint32_t issued = 0, last_parity = 0;
-      for (int j = 0; j < n && !*abort; ++j) {
-        const int st = j % kKV;
-        const uint32_t ph = static_cast<uint32_t>(j / kKV) & 1u;
-        if (!mbar_wait(&s.k_empty[st], ph ^ 1u, abort, err, kSiteLoadEmpty)) break;
-        mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
-        tma_load_3d(s.k[st], &tm_k, &s.k_full[st], 0, j * BK, bh);
-        tma_load_3d(s.k[st] + kBoxBytes, &tm_k, &s.k_full[st], 64, j * BK, bh);
+      for (int t = 0; t < n && !*abort; ++t) {
+        const int st = t % stages;
+        const uint32_t ph = static_cast<uint32_t>(t / stages) & 1u;
+        if (!mbar_wait(&empty[st], ph ^ 1u, abort, err, kSiteLoadEmpty)) break;
+        uint8_t* dst = keys ? s.k[st] : s.v[st];
+        mbar_arrive_expect_tx(&full[st], kTileBytes);
+        tma_load_3d(dst, map, &full[st], 0, t * BK, bh);
+        tma_load_3d(dst + kBoxBytes, map, &full[st], 64, t * BK, bh);
         issued |= 1u << st;
         last_parity = (last_parity & ~(1u << st)) | (ph << st);
-        if (!mbar_wait(&s.v_empty[st], ph ^ 1u, abort, err, kSiteLoadEmpty)) break;
-        mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
-        tma_load_3d(s.v[st], &tm_v, &s.v_full[st], 0, j * BK, bh);
-        tma_load_3d(s.v[st] + kBoxBytes, &tm_v, &s.v_full[st], 64, j * BK, bh);
-        issued |= 1u << (st + kKV);
-        last_parity = (last_parity & ~(1u << (st + kKV))) | (ph << (st + kKV));
       }
       // no copy may still be landing when the CTA leaves (on the normal path the MMA thread consumed them all)
-      mbar_wait_drain(&s.q_full, 0);
-      for (int st = 0; st < kKV; ++st) {
-        if (issued & (1u << st)) mbar_wait_drain(&s.k_full[st], (last_parity >> st) & 1u);
-        if (issued & (1u << (st + kKV))) mbar_wait_drain(&s.v_full[st], (last_parity >> (st + kKV)) & 1u);
-      }
+      if (keys) mbar_wait_drain(&s.q_full, 0);
+      for (int st = 0; st < stages; ++st)
+        if (issued & (1u << st)) mbar_wait_drain(&full[st], (last_parity >> st) & 1u);
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc_s = umma_idesc_bf16(BQ, BK);                 // both K-major
+      const uint32_t idesc_s = umma_idesc_bf16(BQ, BK);                     // both K-major
       const uint32_t idesc_o = umma_idesc_bf16(BQ, kHeadDim) | (1u << 16);  // B (v) MN-major
-      auto issue_scores = [&](int j) -> bool {
-        const int st = j % kKV;
-        if (!mbar_wait(&s.k_full[st], static_cast<uint32_t>(j / kKV) & 1u, abort, err, kSiteScores)) return false;
+      auto issue_scores = [&](int t) -> bool {
+        const int st = t % kK;
+        if (!mbar_wait(&s.k_full[st], static_cast<uint32_t>(t / kK) & 1u, abort, err, kSiteScores)) return false;
         tc_fence_after();
-        const uint32_t d = tmem + col_s(j);
+        const uint32_t d = tmem + col_s(t);
         const uint32_t qa = smem_u32(s.q), kb = smem_u32(s.k[st]);
 #pragma unroll
         for (int kk = 0; kk < kHeadDim / 16; ++kk) {  // 16 dims a step: 32 bytes inside a swizzle atom
@@ -227,108 +307,76 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_mma_f16(d, umma_desc_sw128(qa + off), umma_desc_sw128(kb + off), idesc_s, kk > 0 ? 1u : 0u);
         }
         tc_commit(&s.k_empty[st]);
-        tc_commit(&s.s_full[j & 1]);
+        tc_commit(&s.s_full[t % kSB]);
         return true;
       };
       bool ok = mbar_wait(&s.q_full, 0, abort, err, kSiteQuery);
-      if (ok) {
+      if (ok) tc_fence_after();
+      for (int t = 0; t < kSB && t < n && ok; ++t) ok = issue_scores(t);
+      for (int t = 0; t < n && ok; ++t) {
+        if (!mbar_poll(&s.p_full[t % kSB], static_cast<uint32_t>(t / kSB) & 1u, abort, err, kSiteProbs)) break;
+        const int st = t % kV;
+        if (!mbar_wait(&s.v_full[st], static_cast<uint32_t>(t / kV) & 1u, abort, err, kSiteValues)) break;
         tc_fence_after();
-        ok = issue_scores(0);
-      }
-      if (ok && n > 1) ok = issue_scores(1);
-      for (int j = 0; j < n && ok; ++j) {
-        if (!mbar_wait(&s.p_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u, abort, err, kSiteProbs)) break;
-        const int st = j % kKV;
-        if (!mbar_wait(&s.v_full[st], static_cast<uint32_t>(j / kKV) & 1u, abort, err, kSiteValues)) break;
-        tc_fence_after();
-        const uint32_t a = tmem + col_s(j);  // P_j: 64 columns of bf16 pairs, keys 2c and 2c + 1 in column c
+        const uint32_t a = tmem + col_s(t);  // P: 64 columns of bf16 pairs, keys 2c and 2c + 1 in column c
         const uint32_t vb = smem_u32(s.v[st]);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)  // 16 keys a step: two 8-key groups of 1 KB
           tc_mma_ts(tmem + kColO, a + kk * 8, umma_desc_mn_sw128(vb + kk * 2048, kBoxBytes, 1024), idesc_o,
-                    (j > 0 || kk > 0) ? 1u : 0u);
+                    (t > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&s.v_empty[st]);
         tc_commit(&s.o_done);
-        if (j + 2 < n) ok = issue_scores(j + 2);
+        if (t + kSB < n) ok = issue_scores(t + kSB);
       }
       tc_commit(&s.drain);
       mbar_wait_drain(&s.drain, 0);
     }
-  } else if (warp >= kSoftWarp0) {
+  } else {
     // ---------------- softmax, then the output ----------------
-    const int sw = warp - kSoftWarp0;
-    const int row = sw * 32 + lane;
-    const uint32_t lanes = static_cast<uint32_t>(sw * 32) << 16;
+    const int row = warp * 32 + lane;
+    const uint32_t lanes = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t ob = tmem + lanes + kColO;
     float m = 0.0f, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      if (!warp_wait(&s.s_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u, abort, err, kSiteScores)) {
+    for (int t = 0; t < n; ++t) {
+      if (!warp_wait(&s.s_full[t % kSB], static_cast<uint32_t>(t / kSB) & 1u, abort, err, kSiteScores)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t sb = tmem + lanes + col_s(j);
-      uint32_t r[BK];
-#pragma unroll
-      for (int c = 0; c < BK / 32; ++c) tmem_ld_32(sb + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
-      tmem_wait_ld();
-      const int valid = seq - j * BK;  // keys of this tile inside the sequence
-      if (valid < BK) {
-#pragma unroll
-        for (int i = 0; i < BK; ++i)
-          if (i >= valid) r[i] = 0xFF800000u;  // -inf: P = 0
-      }
-      float mx8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(r[i]);
-#pragma unroll
-      for (int i = 8; i < BK; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(r[i]));
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      const float mt = mx * c_log2;
-      float alpha = 1.0f;
-      if (j == 0) {
-        m = mt;
-      } else if (mt > m + kLazyLog2) {
-        alpha = ex2(m - mt);
-        m = mt;
-      }
+      const uint32_t sb = tmem + lanes + col_s(t);
+      const int valid = seq - t * BK;  // keys of this tile inside the sequence
       uint32_t p[BK / 2];
-      float sum4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-      for (int i = 0; i < BK / 2; ++i) {
-        const float e0 = ex2(fmaf(__uint_as_float(r[2 * i]), c_log2, -m));
-        const float e1 = ex2(fmaf(__uint_as_float(r[2 * i + 1]), c_log2, -m));
-        sum4[i & 3] += e0 + e1;
-        p[i] = pack_bf16x2(e0, e1);
-      }
-      l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-      if (j > 0) {
-        // P_{j-1} v_{j-1} complete: O is whole (for a rescale), and nothing reads the buffer P_j goes to
-        if (!warp_wait(&s.o_done, static_cast<uint32_t>(j - 1) & 1u, abort, err, kSiteOut)) {
+      float alpha;
+      const float sum = valid < BK ? softmax_tile<true>(sb, valid, c_log2, t == 0, m, alpha, p)
+                                   : softmax_tile<false>(sb, valid, c_log2, t == 0, m, alpha, p);
+      l = fmaf(l, alpha, sum);
+      tmem_st_32(sb, p);
+      tmem_st_32(sb + 32, p + 32);
+      if (t > 0) {
+        // P_{t-1} v_{t-1} complete: O is whole for a rescale
+        if (!warp_wait(&s.o_done, static_cast<uint32_t>(t - 1) & 1u, abort, err, kSiteOut)) {
           ok = false;
+          tmem_wait_st();
           break;
         }
         tc_fence_after();
         if (__any_sync(0xFFFFFFFFu, alpha != 1.0f)) {
-          const uint32_t ob = tmem + lanes + kColO;
 #pragma unroll 1
           for (int c = 0; c < kHeadDim / 32; ++c) {
-            uint32_t t[32];
-            tmem_ld_32(ob + c * 32, t);
+            uint32_t x[32];
+            tmem_ld_32(ob + c * 32, x);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
-            tmem_st_32(ob + c * 32, t);
+            for (int k = 0; k < 32; ++k) x[k] = __float_as_uint(__uint_as_float(x[k]) * alpha);
+            tmem_st_32(ob + c * 32, x);
           }
         }
       }
-      tmem_st_32(sb, p);
-      tmem_st_32(sb + 32, p + 32);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.p_full[j & 1]);
+      if (lane == 0) mbar_arrive(&s.p_full[t % kSB]);
     }
     if (ok && warp_wait(&s.o_done, static_cast<uint32_t>(n - 1) & 1u, abort, err, kSiteOut)) {
       tc_fence_after();
@@ -337,16 +385,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint4* dst = reinterpret_cast<uint4*>(o + (static_cast<int64_t>(bh) * seq + qrow) * kHeadDim);
 #pragma unroll 1
       for (int c = 0; c < kHeadDim / 32; ++c) {
-        uint32_t t[32];
-        tmem_ld_32(tmem + lanes + kColO + c * 32, t);
+        uint32_t x[32];
+        tmem_ld_32(ob + c * 32, x);
         tmem_wait_ld();
         uint32_t h[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          h[i] = pack_bf16x2(__uint_as_float(t[2 * i]) * inv, __uint_as_float(t[2 * i + 1]) * inv);
+        for (int k = 0; k < 16; ++k)
+          h[k] = pack_bf16x2(__uint_as_float(x[2 * k]) * inv, __uint_as_float(x[2 * k + 1]) * inv);
         if (qrow < seq) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[c * 4 + i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+          for (int k = 0; k < 4; ++k) dst[c * 4 + k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
         }
       }
     }
@@ -355,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }

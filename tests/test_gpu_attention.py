@@ -6,8 +6,8 @@ fused kernel does, TiledAttention.swift:570-576) and o to bf16, so the bars are:
 <= 4e-3, of every head <= 6e-3, and max-abs <= 2^-6 * max|v| (about 1.6e-3 relative L2 expected from the two
 roundings).  The library attention (torch's fused SDPA on the same bf16 inputs) meets the same bars, and the
 two must agree within them.  Shapes: ragged sequences (the last key tile and the last query tile partly past
-the sequence), peaked scores whose row maximum keeps rising along the keys (the lazy rescale of O runs), and
-configs 3 and 5 at their benchmarked sizes.
+the sequence), peaked scores whose row maximum keeps rising along the keys, and rising far enough that the kernel
+takes the maximum again and rescales O, and configs 3 and 5 at their benchmarked sizes.
 """
 import math
 
@@ -77,12 +77,24 @@ def test_attention_matches_fp32(b, h, s):
 
 def test_attention_with_rising_peaks_rescales():
     """Scores that grow along the keys (k's norm rising with the position) and a sharp softmax: each key tile
-    raises the rows' maximum by more than the lazy threshold, so O is rescaled tile after tile."""
+    raises the rows' maximum, and the later tiles' exponentials under the first tile's maximum run far above 1
+    (kept as they are while their sum stays below the kernel's threshold)."""
     b, h, s = 1, 4, 1024
     q, k, v = operands(b, h, s, seed=3, q_scale=2.0)
     ramp = torch.linspace(0.5, 3.0, s, device="cuda").view(1, 1, s, 1)
     k = (k.float() * ramp).to(torch.bfloat16)
     check(ours(q, k, v), reference(q, k, v), v, "rising peaks")
+
+
+def test_attention_with_a_maximum_that_jumps_far():
+    """Scores whose row maximum rises by far more than 2^32 across the keys (q scaled by 4, k's norm rising 0.25 ->
+    4): the tiles' sums cross the threshold at which the kernel takes the maximum again, redoes the tile and
+    rescales O; keys past the sequence in the last tile too."""
+    b, h, s = 1, 2, 1000
+    q, k, v = operands(b, h, s, seed=5, q_scale=4.0)
+    ramp = torch.linspace(0.25, 4.0, s, device="cuda").view(1, 1, s, 1)
+    k = (k.float() * ramp).to(torch.bfloat16)
+    check(ours(q, k, v), reference(q, k, v), v, "jumping maximum")
 
 
 def test_attention_is_deterministic_and_agrees_with_the_library():
