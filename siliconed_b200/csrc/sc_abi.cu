@@ -284,6 +284,13 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
     return check_cuda(ctx, launch_gemm_skinny(tmx, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
                       "skinny gemm launch");
   }
+  if (m <= 128 && w->n_pad / 256 < ctx->sm_count) {
+    // 32 < m <= 128 with too few 128 x 256 output tiles to fill the SMs (every weight but the widest): the
+    // cluster kernel, whose CTAs split K and own 128 columns each
+    if ((s = make_tmap_x(ctx, x, m, w->k, &tmx, gemm_skinny_box_rows(m))) != SC_OK) return s;
+    return check_cuda(ctx, launch_gemm_skinny(tmx, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
+                      "skinny gemm launch");
+  }
   if ((s = make_tmap_x(ctx, x, m, w->k, &tmx)) != SC_OK) return s;
   if (m > kPairMinRows) {
     // With a workspace for the widened weight: widen once, then the bf16-operand pair GEMM (the

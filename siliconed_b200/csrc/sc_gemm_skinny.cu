@@ -1,8 +1,9 @@
-// The skinny product on the tensor cores: 4 < m <= 32 activation rows (encoder prompts, batched
-// decode), where the GEMV's CUDA-core arithmetic, not HBM, sets the pace.
+// The skinny product on the tensor cores: 4 < m <= 128 activation rows (encoder prompts, batched
+// decode), where the GEMV's CUDA-core arithmetic, not HBM, sets the pace, and where 128 x 256 output
+// tiles would leave most SMs idle (an encoder's [9728, 2560] at 128 rows is 38 such tiles).
 //
-// Operands swapped: the MMA's M is 128 weight columns (output n), its N the m tokens padded to 16 or
-// 32, so D[n, t] = sum_k W[k, n] x[t, k] sits in TMEM with one output column per lane.  A CTA owns
+// Operands swapped: the MMA's M is 128 weight columns (output n), its N the m tokens padded to 16, 32,
+// 64 or 128, so D[n, t] = sum_k W[k, n] x[t, k] sits in TMEM with one output column per lane.  A CTA owns
 // 128 output columns and one K part; the KS CTAs of a cluster (KS in {1, 2, 4, 8}) take the K parts
 // of the same columns, so every SM streams codes even when N / 128 is small.  Per 64-wide K stage:
 // TMA brings the x tile (bf16 [MT x 64], 128-byte swizzle) and the code tile (bytes [128 x 64]),
@@ -22,8 +23,10 @@ namespace sc {
 namespace gemm_skinny {
 
 constexpr int BN = 128, BK = 64;  // weight columns per CTA (the MMA's M), K per stage
-constexpr int kStagesIn = 4;      // x + code tiles in flight
 constexpr int kStagesB = 2;       // converted bf16 weight tiles
+// x + code tiles in flight: 4, or 3 for 128 tokens (16 KB x tiles), so that two CTAs share an SM
+template <int MT>
+constexpr int stages_in() { return MT >= 128 ? 3 : 4; }
 constexpr int kWBytes = BN * BK;
 constexpr int kBBytes = BN * BK * 2;
 constexpr int kWarps = 16;
@@ -31,18 +34,24 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kEpiWarp0 = 4, kEpiWarps = 4;
 constexpr int kConvWarp0 = 8, kConvWarps = 8;
 constexpr int kConvThreads = kConvWarps * 32;
-constexpr uint32_t kTmemCols = 32;
-constexpr int kMaxTokens = 32;
 constexpr int kChunksPerStage = BN * BK / 16;
 
 static_assert(kChunksPerStage % kConvThreads == 0, "converter work must divide evenly");
 static_assert(kThreads == 4 * BN, "the reduction gives each column four threads");
 
+template <int MT>
 struct __align__(1024) Smem {
-  uint8_t b[kStagesB][kBBytes];                 // converted weight tiles (the MMA's A), swizzled
-  uint8_t a[kStagesIn][kMaxTokens * BK * 2];    // x tiles (the MMA's B), swizzled (TMA)
-  uint8_t w[kStagesIn][kWBytes];                // code tiles (TMA)
-  float part[BN][kMaxTokens + 4];               // this CTA's partial D (rows padded to 16-byte units)
+  static constexpr int kStagesIn = stages_in<MT>();
+  union {
+    struct {
+      uint8_t b[kStagesB][kBBytes];           // converted weight tiles (the MMA's A), swizzled
+      uint8_t a[kStagesIn][MT * BK * 2];      // x tiles (the MMA's B), swizzled (TMA)
+      uint8_t w[kStagesIn][kWBytes];          // code tiles (TMA)
+    };
+    // This CTA's partial D (rows padded to 16-byte units), written once the last MMA has completed, when no
+    // copy or conversion writes the pipeline's buffers any more.
+    float part[BN][MT + 4];
+  };
   uint64_t in_full[kStagesIn];
   uint64_t in_empty[kStagesIn];
   uint64_t b_full[kStagesB];
@@ -53,7 +62,9 @@ struct __align__(1024) Smem {
   int abort;
 };
 
-constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+template <int MT>
+constexpr size_t smem_bytes() { return sizeof(Smem<MT>) + 1024; }
+static_assert(smem_bytes<128>() <= 113 * 1024 && smem_bytes<64>() <= 113 * 1024, "two CTAs an SM");
 
 __device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t cluster_addr) {
   float4 v;
@@ -69,8 +80,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     gemm_w8_skinny(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const float* __restrict__ scales, const uint16_t* __restrict__ bias, void* __restrict__ y_out,
                    int M, int N, int k_tiles, int* err) {
+  constexpr int kStagesIn = Smem<MT>::kStagesIn;
+  constexpr uint32_t kTmemCols = MT < 32 ? 32u : static_cast<uint32_t>(MT);
   extern __shared__ uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Smem<MT>& s = *reinterpret_cast<Smem<MT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   uint32_t ks_count;
@@ -169,11 +182,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int col = ew * 32 + lane;
     if (got) {
       tc_fence_after();
-      uint32_t r[32];
-      tmem_ld_32(tmem + (static_cast<uint32_t>(ew * 32) << 16), r);
-      tmem_wait_ld();
+#pragma unroll 1
+      for (int c = 0; c < (MT + 31) / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32(tmem + (static_cast<uint32_t>(ew * 32) << 16) + c * 32, r);
+        tmem_wait_ld();
 #pragma unroll
-      for (int t = 0; t < MT; ++t) s.part[col][t] = __uint_as_float(r[t]);
+        for (int t = 0; t < 32; ++t)
+          if (c * 32 + t < MT) s.part[col][c * 32 + t] = __uint_as_float(r[t]);
+      }
     } else {
 #pragma unroll
       for (int t = 0; t < MT; ++t) s.part[col][t] = 0.0f;
@@ -224,35 +241,39 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before();
   cluster_barrier();
   if (rank == 0) {
-    constexpr int TPG = MT / 4;  // tokens per thread
+    constexpr int TPG = MT / 4;            // tokens per thread
+    constexpr int TC = TPG < 8 ? TPG : 8;  // ... added a chunk at a time
     const int col = threadIdx.x % BN, t0 = (threadIdx.x / BN) * TPG;
     const int n = tile * BN + col;
-    float acc[TPG];
+    const float sc = n < N ? scales[n] : 0.0f;
+    const float b = (n < N && bias != nullptr) ? __uint_as_float(static_cast<uint32_t>(bias[n]) << 16) : 0.0f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < TPG; c0 += TC) {
+      float acc[TC];
 #pragma unroll
-    for (int i = 0; i < TPG; ++i) acc[i] = s.part[col][t0 + i];
-    for (uint32_t q = 1; q < ks_count; ++q) {
-      const uint32_t base = peer_addr(&s.part[col][t0], q);
-      float4 v[TPG / 4];
+      for (int i = 0; i < TC; ++i) acc[i] = s.part[col][t0 + c0 + i];
+      for (uint32_t q = 1; q < ks_count; ++q) {
+        const uint32_t base = peer_addr(&s.part[col][t0 + c0], q);
+        float4 v[TC / 4];
 #pragma unroll
-      for (int i = 0; i < TPG / 4; ++i) v[i] = ld_dsmem_f32x4(base + 16u * i);
+        for (int i = 0; i < TC / 4; ++i) v[i] = ld_dsmem_f32x4(base + 16u * i);
 #pragma unroll
-      for (int i = 0; i < TPG / 4; ++i) {
-        acc[4 * i] = __fadd_rn(acc[4 * i], v[i].x);
-        acc[4 * i + 1] = __fadd_rn(acc[4 * i + 1], v[i].y);
-        acc[4 * i + 2] = __fadd_rn(acc[4 * i + 2], v[i].z);
-        acc[4 * i + 3] = __fadd_rn(acc[4 * i + 3], v[i].w);
+        for (int i = 0; i < TC / 4; ++i) {
+          acc[4 * i] = __fadd_rn(acc[4 * i], v[i].x);
+          acc[4 * i + 1] = __fadd_rn(acc[4 * i + 1], v[i].y);
+          acc[4 * i + 2] = __fadd_rn(acc[4 * i + 2], v[i].z);
+          acc[4 * i + 3] = __fadd_rn(acc[4 * i + 3], v[i].w);
+        }
       }
-    }
-    if (n < N) {
-      const float sc = scales[n];
-      const float b = bias != nullptr ? __uint_as_float(static_cast<uint32_t>(bias[n]) << 16) : 0.0f;
+      if (n < N) {
 #pragma unroll
-      for (int i = 0; i < TPG; ++i) {
-        const int t = t0 + i;
-        if (t < M) {
-          const float v = __fadd_rn(__fmul_rn(acc[i], sc), b);
-          if (kF32Out) static_cast<float*>(y_out)[static_cast<int64_t>(t) * N + n] = v;
-          else static_cast<uint16_t*>(y_out)[static_cast<int64_t>(t) * N + n] = f32_to_bf16_rne(v);
+        for (int i = 0; i < TC; ++i) {
+          const int t = t0 + c0 + i;
+          if (t < M) {
+            const float v = __fadd_rn(__fmul_rn(acc[i], sc), b);
+            if (kF32Out) static_cast<float*>(y_out)[static_cast<int64_t>(t) * N + n] = v;
+            else static_cast<uint16_t*>(y_out)[static_cast<int64_t>(t) * N + n] = f32_to_bf16_rne(v);
+          }
         }
       }
     }
@@ -270,7 +291,7 @@ cudaError_t launch_mt(const CUtensorMap& tm_x, const sc_weight* w, const uint16_
                       int sm_count, cudaStream_t stream) {
   auto kernel = gemm_w8_skinny<kKind, kNaN, kF32Out, MT>;
   static unsigned long long configured = 0;  // per template instance and device
-  if (cudaError_t e = set_smem_once(kernel, static_cast<int>(kSmemBytes), configured); e != cudaSuccess) return e;
+  if (cudaError_t e = set_smem_once(kernel, static_cast<int>(smem_bytes<MT>()), configured); e != cudaSuccess) return e;
   const int n_tiles = static_cast<int>(w->n_pad / BN);
   const int k_tiles = static_cast<int>(w->k_pad / BK);
   int ks = 1;
@@ -278,7 +299,7 @@ cudaError_t launch_mt(const CUtensorMap& tm_x, const sc_weight* w, const uint16_
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * ks), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = smem_bytes<MT>();
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -295,12 +316,14 @@ template <int kKind, bool kNaN, bool kF32Out>
 cudaError_t launch_kind(const CUtensorMap& tm_x, const sc_weight* w, const uint16_t* bias, void* y, int64_t m, int* err,
                         int sm_count, cudaStream_t stream) {
   if (m <= 16) return launch_mt<kKind, kNaN, kF32Out, 16>(tm_x, w, bias, y, m, err, sm_count, stream);
-  return launch_mt<kKind, kNaN, kF32Out, 32>(tm_x, w, bias, y, m, err, sm_count, stream);
+  if (m <= 32) return launch_mt<kKind, kNaN, kF32Out, 32>(tm_x, w, bias, y, m, err, sm_count, stream);
+  if (m <= 64) return launch_mt<kKind, kNaN, kF32Out, 64>(tm_x, w, bias, y, m, err, sm_count, stream);
+  return launch_mt<kKind, kNaN, kF32Out, 128>(tm_x, w, bias, y, m, err, sm_count, stream);
 }
 
 }  // namespace gemm_skinny
 
-int gemm_skinny_box_rows(int64_t m) { return m <= 16 ? 16 : 32; }
+int gemm_skinny_box_rows(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128; }
 
 cudaError_t launch_gemm_skinny(const CUtensorMap& tmap_x, const sc_weight* w, const uint16_t* bias, void* y,
                                bool f32_out, int64_t m, int* err, int sm_count, cudaStream_t stream) {

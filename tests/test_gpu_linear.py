@@ -299,6 +299,26 @@ def test_int8_products_of_17_to_32_rows_take_no_workspace(ctx):
     check_against_oracle(ctx, abi.WEIGHT_INT8, x, q, s, None, "int8 m=20")
 
 
+@pytest.mark.parametrize("kind,m", [(abi.WEIGHT_INT8, 33), (abi.WEIGHT_INT8, 64), (abi.WEIGHT_INT8, 100),
+                                    (abi.WEIGHT_INT8, 128), (abi.WEIGHT_E4M3, 80)])
+def test_prefill_rows_on_the_cluster_kernel_match_the_oracle(ctx, kind, m):
+    """32 < m <= 128 on a weight too narrow for 148 output tiles of 128 x 256 (the Z-Image encoder's gate / up
+    shape, [9728, 2560] published): the cluster kernel with 64 or 128 token columns, K split over the cluster's
+    CTAs and added in rank order."""
+    k, n = 2560, 9728
+    g = np.random.default_rng(900 + m)
+    x = configs.to_bf16_bits(g.standard_normal((m, k), dtype=np.float32))
+    if kind == abi.WEIGHT_INT8:
+        q = g.integers(-128, 128, (k, n), dtype=np.int16).astype(np.int8).view(np.uint8)
+        s = (np.abs(g.standard_normal(n)) * 0.02 / 127 + 1e-6).astype(np.float32)
+    else:
+        q = configs.to_e4m3_codes(g.standard_normal((k, n), dtype=np.float32) * 4)
+        q[(q & 0x7F) == 0x7F] ^= 1
+        s = (np.abs(g.standard_normal(n)) * 0.02 / 448 + 1e-6).astype(np.float32)
+    b = configs.to_bf16_bits(g.standard_normal(n, dtype=np.float32) * 0.01)
+    check_against_oracle(ctx, kind, x, q, s, b, f"prefill m={m}")
+
+
 def test_int8_skinny_product_with_zero_and_nonfinite_rows(ctx):
     """A row of x that is all zeros gives the bias; a row holding an infinity gives NaN (its products meet
     weights of both signs); the other rows are unaffected."""
