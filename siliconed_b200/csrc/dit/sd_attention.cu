@@ -12,15 +12,17 @@
 //
 // One CTA per 128 query rows of one head (the grid's CTAs of one head consecutive, so the head's k and v stay in
 // L2 while they are read).  Roles:
-// - warp 4: TMA.  Lane 0 loads the q tile once ([128 rows][128 dims] as two 128-byte-swizzled boxes of 64 dims)
-//   and the k tiles of 128 keys through a ring of three 32 KB stages; lane 1 the v tiles through a ring of two (v
-//   is needed later than k).  Coordinates past seq read zeros.
-// - warp 5, one thread: the MMAs.  S_t = q k_t^T (tcgen05.mma kind::f16, M 128, N 128, both operands K-major from
-//   shared memory) into one of three TMEM buffers of 128 fp32 columns, three key tiles ahead of the softmax (with
-//   two, S_{t+1} could only start once P_{t-1} v had read its buffer, which chained every softmax to the MMAs of
-//   the tile before); then O += P_t v_t with P_t read from TMEM (the A operand, bf16 pairs in the S buffer's first
-//   64 columns) and v_t from shared memory as an MN-major B operand (its 128-byte rows are keys, 64 dims each:
-//   LBO = the 16 KB between the two dim halves, SBO = 1 KB between 8-key groups).  TMEM: S_0, S_1, S_2, O.
+// - warps 0-3 first write the q tile into TMEM (each thread its row: 128 bf16 as 64 columns of pairs, read from
+//   global memory), where it is the A operand of every S MMA: S = q k^T then reads only k from shared memory.
+//   With both operands in shared memory the S MMAs (8 KB of operands each) ran at about 60 % of the tensor rate,
+//   bound by shared-memory bandwidth beside the TMA's writes of k and v.
+// - warp 4: TMA.  Lane 0 loads the k tiles of 128 keys through a ring of three 32 KB stages, lane 1 the v tiles
+//   through a ring of three.  Coordinates past seq read zeros.
+// - warp 5, one thread: the MMAs.  S_t = q k_t^T (tcgen05.mma kind::f16, M 128, N 128, A from TMEM, B K-major
+//   from shared memory) into one of two TMEM buffers of 128 fp32 columns, two key tiles ahead of the softmax;
+//   then O += P_t v_t with P_t read from TMEM (the A operand, bf16 pairs in the S buffer's first 64 columns) and
+//   v_t from shared memory as an MN-major B operand (its 128-byte rows are keys, 64 dims each: LBO = the 16 KB
+//   between the two dim halves, SBO = 1 KB between 8-key groups).  TMEM: S_0, S_1, O, q.
 // - warps 0-3: the softmax, one query row per thread (TMEM lane = row).  Each reads its row of S 32 columns at a
 //   time (the next load in flight while the last is used) and forms exp2(s c - m) with the row's running maximum m
 //   (c = scale log2 e; ex2.approx), their sum and their bf16 pairs.  The maximum itself is only taken when the
@@ -48,25 +50,25 @@ using namespace sc;
 constexpr int kHeadDim = 128;
 constexpr int BQ = 128;                         // query rows a CTA
 constexpr int BK = 128;                         // keys a tile
-constexpr int kK = 3, kV = 2;                   // ring stages for k and for v
+constexpr int kK = 3, kV = 3;                   // ring stages for k and for v
 constexpr int kTileBytes = BK * kHeadDim * 2;   // 32 KB
 constexpr int kBoxBytes = kTileBytes / 2;       // [128 rows][64 dims], 16 KB
 constexpr int kThreads = 192;                   // warps 0-3 softmax, 4 TMA, 5 MMA
 constexpr int kTmaWarp = 4, kMmaWarp = 5;
-constexpr int kSB = 3;                          // S / P buffers in TMEM
+constexpr int kSB = 2;                          // S / P buffers in TMEM
 constexpr float kMovedSum = 4294967296.0f;      // 2^32: a tile's sum above it means the maximum moved
 constexpr uint32_t kTmemCols = 512;
 
 __device__ __forceinline__ uint32_t col_s(int t) { return static_cast<uint32_t>(t % kSB) * 128u; }  // S_t; P_t: first 64
-constexpr uint32_t kColO = 384;                                                                    // O: 128 columns
+constexpr uint32_t kColO = 256;                                                                    // O: 128 columns
+constexpr uint32_t kColQ = 384;                                                                    // q: 64 columns
 
 enum : int { kSiteLoadEmpty = 21, kSiteScores = 22, kSiteProbs = 23, kSiteValues = 24, kSiteQuery = 25, kSiteOut = 26 };
 
 struct __align__(1024) Smem {
-  uint8_t q[kTileBytes];
   uint8_t k[kK][kTileBytes];
   uint8_t v[kV][kTileBytes];
-  uint64_t q_full;
+  uint64_t q_ready;      // q written into TMEM (one arrival per softmax warp)
   uint64_t k_full[kK], k_empty[kK];
   uint64_t v_full[kV], v_empty[kV];
   uint64_t s_full[kSB];  // S_t complete in buffer t % 3 (MMA -> softmax)
@@ -219,7 +221,7 @@ __device__ __forceinline__ float softmax_tile(uint32_t sb, int valid, float c_lo
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    attention_fwd(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    attention_fwd(const uint16_t* __restrict__ q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, uint16_t* __restrict__ o, int seq, int q_tiles,
                   float c_log2, int* err) {
   extern __shared__ uint8_t smem_raw[];
@@ -230,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = &s.abort;
 
   if (threadIdx.x == 0) {
-    mbar_init(&s.q_full, 1);
+    mbar_init(&s.q_ready, 4);
     for (int i = 0; i < kK; ++i) {
       mbar_init(&s.k_full[i], 1);
       mbar_init(&s.k_empty[i], 1);
@@ -247,7 +249,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&s.drain, 1);
     s.abort = 0;
     fence_mbar_init();
-    prefetch_tensormap(&tm_q);
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
   }
@@ -268,11 +269,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* full = keys ? s.k_full : s.v_full;
       uint64_t* empty = keys ? s.k_empty : s.v_empty;
       const CUtensorMap* map = keys ? &tm_k : &tm_v;
-      if (keys) {
-        mbar_arrive_expect_tx(&s.q_full, kTileBytes);
-        tma_load_3d(s.q, &tm_q, &s.q_full, 0, q0, bh);
-        tma_load_3d(s.q + kBoxBytes, &tm_q, &s.q_full, 64, q0, bh);
-      }
       uint32_t issued = 0, last_parity = 0;
       for (int t = 0; t < n && !*abort; ++t) {
         const int st = t % stages;
@@ -286,7 +282,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         last_parity = (last_parity & ~(1u << st)) | (ph << st);
       }
       // no copy may still be landing when the CTA leaves (on the normal path the MMA thread consumed them all)
-      if (keys) mbar_wait_drain(&s.q_full, 0);
       for (int st = 0; st < stages; ++st)
         if (issued & (1u << st)) mbar_wait_drain(&full[st], (last_parity >> st) & 1u);
     }
@@ -300,17 +295,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&s.k_full[st], static_cast<uint32_t>(t / kK) & 1u, abort, err, kSiteScores)) return false;
         tc_fence_after();
         const uint32_t d = tmem + col_s(t);
-        const uint32_t qa = smem_u32(s.q), kb = smem_u32(s.k[st]);
+        const uint32_t kb = smem_u32(s.k[st]);
 #pragma unroll
-        for (int kk = 0; kk < kHeadDim / 16; ++kk) {  // 16 dims a step: 32 bytes inside a swizzle atom
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {  // 16 dims a step: 8 columns of q, 32 bytes of k's swizzle atom
           const uint32_t off = static_cast<uint32_t>((kk >> 2) * kBoxBytes + (kk & 3) * 32);
-          tc_mma_f16(d, umma_desc_sw128(qa + off), umma_desc_sw128(kb + off), idesc_s, kk > 0 ? 1u : 0u);
+          tc_mma_ts(d, tmem + kColQ + kk * 8, umma_desc_sw128(kb + off), idesc_s, kk > 0 ? 1u : 0u);
         }
         tc_commit(&s.k_empty[st]);
         tc_commit(&s.s_full[t % kSB]);
         return true;
       };
-      bool ok = mbar_wait(&s.q_full, 0, abort, err, kSiteQuery);
+      bool ok = mbar_poll(&s.q_ready, 0, abort, err, kSiteQuery);
       if (ok) tc_fence_after();
       for (int t = 0; t < kSB && t < n && ok; ++t) ok = issue_scores(t);
       for (int t = 0; t < n && ok; ++t) {
@@ -332,10 +327,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_drain(&s.drain, 0);
     }
   } else {
-    // ---------------- softmax, then the output ----------------
+    // ---------------- q into TMEM, the softmax, then the output ----------------
     const int row = warp * 32 + lane;
     const uint32_t lanes = static_cast<uint32_t>(warp * 32) << 16;
     const uint32_t ob = tmem + lanes + kColO;
+    {
+      // this row of q (zeros past seq) as 64 columns of bf16 pairs: dims 2c and 2c + 1 in column c
+      uint32_t qv[kHeadDim / 2];
+      const bool in_seq = q0 + row < seq;
+      const uint4* src = reinterpret_cast<const uint4*>(q + (static_cast<int64_t>(bh) * seq + (in_seq ? q0 + row : 0)) * kHeadDim);
+#pragma unroll
+      for (int i = 0; i < kHeadDim / 8; ++i) {
+        const uint4 v4 = in_seq ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
+        qv[4 * i] = v4.x;
+        qv[4 * i + 1] = v4.y;
+        qv[4 * i + 2] = v4.z;
+        qv[4 * i + 3] = v4.w;
+      }
+      tmem_st_32(tmem + lanes + kColQ, qv);
+      tmem_st_32(tmem + lanes + kColQ + 32, qv + 32);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.q_ready);
+    }
     float m = 0.0f, l = 0.0f;
     bool ok = true;
     for (int t = 0; t < n; ++t) {
@@ -452,9 +467,8 @@ SD_API int sd_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v,
   if (q_tiles * bh > 0x7FFFFFFF) return SD_INVALID_ARG;
   encode_fn enc = encoder();
   if (enc == nullptr) return SD_CUDA_ERROR;
-  CUtensorMap tq, tk, tv;
-  if (!make_map(&tq, enc, q, bh, seq) || !make_map(&tk, enc, k, bh, seq) || !make_map(&tv, enc, v, bh, seq))
-    return SD_INVALID_ARG;
+  CUtensorMap tk, tv;
+  if (!make_map(&tk, enc, k, bh, seq) || !make_map(&tv, enc, v, bh, seq)) return SD_INVALID_ARG;
   static unsigned long long configured = 0;  // one bit per device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return SD_CUDA_ERROR;
@@ -468,7 +482,7 @@ SD_API int sd_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v,
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_attention_err) != cudaSuccess) return SD_CUDA_ERROR;
   const float c_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);  // scale * log2(e)
   attention_fwd<<<static_cast<unsigned>(q_tiles * bh), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
-      tq, tk, tv, o, seq, static_cast<int>(q_tiles), c_log2, err);
+      q, tk, tv, o, seq, static_cast<int>(q_tiles), c_log2, err);
   return cudaGetLastError() == cudaSuccess ? SD_OK : SD_CUDA_ERROR;
 }
 
