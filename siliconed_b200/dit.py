@@ -182,7 +182,7 @@ def image_text_positions(txt_tokens: int, grid: int) -> torch.Tensor:
 
 # "native": sd_attention, this project's tcgen05 kernel (parity-tested at configs 3 and 5); "library": torch's
 # fused scaled-dot-product attention, the default while it is the faster of the two on B200 (config 3's
-# attention: 228 us against 386 us for sd_attention).
+# attention: 228 us against 391 us for sd_attention).
 ATTENTION = "library"
 
 
