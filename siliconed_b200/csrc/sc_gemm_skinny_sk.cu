@@ -358,15 +358,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           __threadfence();
 #pragma unroll
           for (int i = 0; i < MT; ++i) v[i] = 0;
-          for (int c = c_first; c <= c_last; ++c) {  // integer sums: exact in any order
+          // integer sums: exact in any order; plain L2 loads (after the fence above) that the compiler may
+          // issue ahead of the adds, so the CTAs' partials arrive together rather than one round trip each
+#pragma unroll 2
+          for (int c = c_first; c <= c_last; ++c) {
             const int cslot = t == static_cast<int>(share_begin(c, units, grid) / k_tiles) ? 0 : 1;
-            const long long* f = partials + ((static_cast<int64_t>(c) * kSlots + cslot) * BN + row) * kTokens;
+            const longlong2* f = reinterpret_cast<const longlong2*>(
+                partials + ((static_cast<int64_t>(c) * kSlots + cslot) * BN + row) * kTokens);
+            longlong2 x[MT / 2];
 #pragma unroll
-            for (int i = 0; i < MT; i += 2) {
-              long long a, b;
-              asm volatile("ld.global.cg.v2.s64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(f + i));
-              v[i] += a;
-              v[i + 1] += b;
+            for (int i = 0; i < MT / 2; ++i) x[i] = __ldcg(f + i);
+#pragma unroll
+            for (int i = 0; i < MT / 2; ++i) {
+              v[2 * i] += x[i].x;
+              v[2 * i + 1] += x[i].y;
             }
           }
         }
