@@ -37,7 +37,7 @@ constexpr int kConvThreads = kConvWarps * 32;
 constexpr int kChunksPerStage = BN * BK / 16;
 
 static_assert(kChunksPerStage % kConvThreads == 0, "converter work must divide evenly");
-static_assert(kThreads == 4 * BN, "the reduction gives each column four threads");
+static_assert(kThreads == 8 * (BN / 2), "the sums: a column pair and every eighth token a thread");
 
 template <int MT>
 struct __align__(1024) Smem {
@@ -48,9 +48,9 @@ struct __align__(1024) Smem {
       uint8_t a[kStagesIn][MT * BK * 2];      // x tiles (the MMA's B), swizzled (TMA)
       uint8_t w[kStagesIn][kWBytes];          // code tiles (TMA)
     };
-    // This CTA's partial D (rows padded to 16-byte units), written once the last MMA has completed, when no
-    // copy or conversion writes the pipeline's buffers any more.
-    float part[BN][MT + 4];
+    // This CTA's partial D, token-major (rows of the tile's 128 columns, padded to 16-byte units), written once
+    // the last MMA has completed, when no copy or conversion writes the pipeline's buffers any more.
+    float part[MT][BN + 4];
   };
   uint64_t in_full[kStagesIn];
   uint64_t in_empty[kStagesIn];
@@ -66,14 +66,6 @@ template <int MT>
 constexpr size_t smem_bytes() { return sizeof(Smem<MT>) + 1024; }
 static_assert(smem_bytes<128>() <= 113 * 1024 && smem_bytes<64>() <= 113 * 1024, "two CTAs an SM");
 
-__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t cluster_addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(cluster_addr)
-               : "memory");
-  return v;
-}
 
 template <int kKind, bool kNaN, bool kF32Out, int MT>
 __global__ void __launch_bounds__(kThreads, 2)
@@ -189,11 +181,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_wait_ld();
 #pragma unroll
         for (int t = 0; t < 32; ++t)
-          if (c * 32 + t < MT) s.part[col][c * 32 + t] = __uint_as_float(r[t]);
+          if (c * 32 + t < MT) s.part[c * 32 + t][col] = __uint_as_float(r[t]);
       }
     } else {
 #pragma unroll
-      for (int t = 0; t < MT; ++t) s.part[col][t] = 0.0f;
+      for (int t = 0; t < MT; ++t) s.part[t][col] = 0.0f;
     }
   } else if (warp >= kConvWarp0) {
     // ---------------- converters ----------------
@@ -235,50 +227,66 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
 
-  // Every CTA's partial is in its shared memory; the leader's 512 threads add them in rank order
-  // (thread: one column, a quarter of the tokens), reading the peers' rows 16 bytes at a time.
+  // Every CTA's partial is in its shared memory.  Each CTA of the cluster then takes a share of the tokens and
+  // adds the KS partials of its tokens in rank order 0 .. KS - 1 (its own from shared memory, the peers' through
+  // distributed shared memory): the same sums in the same order whichever CTA adds them.  A thread takes a pair
+  // of columns and every eighth token of the share, so a warp reads 256 contiguous bytes of a partial row and
+  // writes 128 contiguous bytes of y.
   __syncwarp();
   tc_fence_before();
   cluster_barrier();
-  if (rank == 0) {
-    constexpr int TPG = MT / 4;            // tokens per thread
-    constexpr int TC = TPG < 8 ? TPG : 8;  // ... added a chunk at a time
-    const int col = threadIdx.x % BN, t0 = (threadIdx.x / BN) * TPG;
-    const int n = tile * BN + col;
-    const float sc = n < N ? scales[n] : 0.0f;
-    const float b = (n < N && bias != nullptr) ? __uint_as_float(static_cast<uint32_t>(bias[n]) << 16) : 0.0f;
-#pragma unroll 1
-    for (int c0 = 0; c0 < TPG; c0 += TC) {
-      float acc[TC];
-#pragma unroll
-      for (int i = 0; i < TC; ++i) acc[i] = s.part[col][t0 + c0 + i];
-      for (uint32_t q = 1; q < ks_count; ++q) {
-        const uint32_t base = peer_addr(&s.part[col][t0 + c0], q);
-        float4 v[TC / 4];
-#pragma unroll
-        for (int i = 0; i < TC / 4; ++i) v[i] = ld_dsmem_f32x4(base + 16u * i);
-#pragma unroll
-        for (int i = 0; i < TC / 4; ++i) {
-          acc[4 * i] = __fadd_rn(acc[4 * i], v[i].x);
-          acc[4 * i + 1] = __fadd_rn(acc[4 * i + 1], v[i].y);
-          acc[4 * i + 2] = __fadd_rn(acc[4 * i + 2], v[i].z);
-          acc[4 * i + 3] = __fadd_rn(acc[4 * i + 3], v[i].w);
+  {
+    const int cp = threadIdx.x % (BN / 2), tg = threadIdx.x / (BN / 2);  // column pair, token group (0..7)
+    const int n = tile * BN + 2 * cp;
+    const int t_lo = static_cast<int>(rank) * MT / static_cast<int>(ks_count);
+    const int t_hi = static_cast<int>(rank + 1) * MT / static_cast<int>(ks_count);
+    const float2 sc = make_float2(n < N ? scales[n] : 0.0f, n + 1 < N ? scales[n + 1] : 0.0f);
+    float2 b = make_float2(0.0f, 0.0f);
+    if (bias != nullptr) {
+      if (n < N) b.x = __uint_as_float(static_cast<uint32_t>(bias[n]) << 16);
+      if (n + 1 < N) b.y = __uint_as_float(static_cast<uint32_t>(bias[n + 1]) << 16);
+    }
+    const bool pair_store = (N & 1) == 0 && n + 1 < N;
+    for (int t = t_lo + tg; t < t_hi && t < M; t += kThreads / (BN / 2)) {
+      float2 acc = make_float2(0.0f, 0.0f);
+      for (uint32_t q = 0; q < ks_count; ++q) {
+        float2 v;
+        if (q == rank) {
+          v = *reinterpret_cast<const float2*>(&s.part[t][2 * cp]);
+        } else {
+          asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];"
+                       : "=f"(v.x), "=f"(v.y)
+                       : "r"(peer_addr(&s.part[t][2 * cp], q))
+                       : "memory");
+        }
+        if (q == 0) {
+          acc = v;
+        } else {
+          acc.x = __fadd_rn(acc.x, v.x);
+          acc.y = __fadd_rn(acc.y, v.y);
         }
       }
-      if (n < N) {
-#pragma unroll
-        for (int i = 0; i < TC; ++i) {
-          const int t = t0 + c0 + i;
-          if (t < M) {
-            const float v = __fadd_rn(__fmul_rn(acc[i], sc), b);
-            if (kF32Out) static_cast<float*>(y_out)[static_cast<int64_t>(t) * N + n] = v;
-            else static_cast<uint16_t*>(y_out)[static_cast<int64_t>(t) * N + n] = f32_to_bf16_rne(v);
-          }
+      const float o0 = __fadd_rn(__fmul_rn(acc.x, sc.x), b.x), o1 = __fadd_rn(__fmul_rn(acc.y, sc.y), b.y);
+      const int64_t off = static_cast<int64_t>(t) * N + n;
+      if (kF32Out) {
+        float* yo = static_cast<float*>(y_out) + off;
+        if (pair_store) *reinterpret_cast<float2*>(yo) = make_float2(o0, o1);
+        else {
+          if (n < N) yo[0] = o0;
+          if (n + 1 < N) yo[1] = o1;
+        }
+      } else {
+        uint16_t* yo = static_cast<uint16_t*>(y_out) + off;
+        if (pair_store) *reinterpret_cast<uint32_t*>(yo) = static_cast<uint32_t>(f32_to_bf16_rne(o0)) |
+                                                            (static_cast<uint32_t>(f32_to_bf16_rne(o1)) << 16);
+        else {
+          if (n < N) yo[0] = f32_to_bf16_rne(o0);
+          if (n + 1 < N) yo[1] = f32_to_bf16_rne(o1);
         }
       }
     }
   }
-  // The peers' partials stay in place until the leader has read them.
+  // Every CTA's partial stays in place until the other CTAs have read it.
   cluster_barrier();
   if (warp == 1) {
     tc_fence_after();
