@@ -59,6 +59,8 @@ struct __align__(1024) Smem {
   uint32_t tmem_base;
   int abort;
   int last;  // the fix-up decision of the current segment, for the epilogue warps
+  int shift[kTokens];         // the rows' shifts and corrections, staged once by the epilogue warps
+  long long corr[kTokens];
 };
 
 template <int MT>
@@ -298,6 +300,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();  // the shifts and corrections are the kernel ahead's output
     const int ew = warp - kEpiWarp0;  // TMEM lanes [32 ew, 32 ew + 32): output columns of the tile
     const int row = ew * 32 + lane;
+    // staged while the main loop runs: the y step then reads them from shared memory, not in a chain of loads
+    if (row < MT) {
+      s.shift[row] = shift[row];
+      s.corr[row] = corr[row];
+    }
+    named_barrier_sync(1, kEpiWarps * 32);
     int acc = 0, seg = 0;
     uint32_t acc_phase = 0;
     for (int64_t u = u0; u < u1; ++seg) {
@@ -305,6 +313,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t tile_end = static_cast<int64_t>(t + 1) * k_tiles;
       const int64_t seg_end = u1 < tile_end ? u1 : tile_end;
       const bool whole = u == static_cast<int64_t>(t) * k_tiles && seg_end == tile_end;
+      // this segment's column: scale and bias requested before the wait for its sums
+      const int n = t * BN + row;
+      const float sc = n < N ? scales[n] : 0.0f;
+      const float b = (n < N && bias != nullptr) ? __uint_as_float(static_cast<uint32_t>(bias[n]) << 16) : 0.0f;
       int got = 0;
       if (lane == 0) got = mbar_wait(&s.acc_full[acc], acc_phase, abort, err, kSiteEpilogueFull) ? 1 : 0;
       got = __shfl_sync(0xFFFFFFFFu, got, 0);
@@ -334,7 +346,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
-      const int n = t * BN + row;
       bool store = whole;
       if (!whole) {
         const int slot = seg == 0 ? 0 : 1;
@@ -377,16 +388,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (store && n < N) {
-        const float sc = scales[n];
-        const float b = bias != nullptr ? __uint_as_float(static_cast<uint32_t>(bias[n]) << 16) : 0.0f;
 #pragma unroll
         for (int i = 0; i < MT; ++i)
           if (i < M) {
-            const int sh = shift[i];
+            const int sh = s.shift[i];
             float sum;
             if (sh == kZeroRow) sum = 0.0f;
             else if (sh == kBadRow) sum = __uint_as_float(0x7FC00000u);
-            else sum = static_cast<float>(ldexp(static_cast<double>(v[i] - corr[i]), sh));  // one rounding
+            else sum = static_cast<float>(ldexp(static_cast<double>(v[i] - s.corr[i]), sh));  // one rounding
             const float o = __fadd_rn(__fmul_rn(sum, sc), b);
             if (kF32Out) static_cast<float*>(y_out)[static_cast<int64_t>(i) * N + n] = o;
             else static_cast<uint16_t*>(y_out)[static_cast<int64_t>(i) * N + n] = f32_to_bf16_rne(o);
