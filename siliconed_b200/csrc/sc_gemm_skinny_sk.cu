@@ -395,7 +395,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             float sum;
             if (sh == kZeroRow) sum = 0.0f;
             else if (sh == kBadRow) sum = __uint_as_float(0x7FC00000u);
-            else sum = static_cast<float>(ldexp(static_cast<double>(v[i] - s.corr[i]), sh));  // one rounding
+            // times 2^sh (sh in [-147, 106]) as a product with that power of two, exact in double; the
+            // conversion to fp32 is the one rounding
+            else sum = __double2float_rn(static_cast<double>(v[i] - s.corr[i]) *
+                                         __longlong_as_double(static_cast<long long>(sh + 1023) << 52));
             const float o = __fadd_rn(__fmul_rn(sum, sc), b);
             if (kF32Out) static_cast<float*>(y_out)[static_cast<int64_t>(i) * N + n] = o;
             else static_cast<uint16_t*>(y_out)[static_cast<int64_t>(i) * N + n] = f32_to_bf16_rne(o);
