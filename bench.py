@@ -151,9 +151,12 @@ class ClockSampler:
 
 def route_kernels(case, ws_bytes: int) -> list[str]:
     """The library's kernels one product of this case launches (the step the roofline's `achieved`
-    covers): the GEMV up to 4 rows, the skinny tensor-core product up to 32, the single-CTA GEMM up
+    covers): the GEMV up to 4 rows (an int8 weight of 3-16 rows with the workspace: the integer skinny
+    product), the skinny tensor-core product up to 32, the single-CTA GEMM up
     to 128 rows, the fused pair kernel above, and from 1536 rows with a workspace the widening of the
     codes followed by the bf16-operand pair GEMM."""
+    if case.m <= 16 and case.m > 2 and case.kind == 1 and ws_bytes > 0:
+        return ["x_planes", "gemm_i8_skinny"]
     if case.m <= 4:
         return ["gemv_w8"]
     if case.m <= 16 and case.kind == 1 and ws_bytes > 0:

@@ -180,8 +180,9 @@ SC_API sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, s
  * (TensorGEMMBF16.swift:43-47).  bias may be NULL.  Replaces TensorGEMM.linear(a:int8:...)
  * (TensorGEMM.swift:264-290) / submitRounded (TensorGEMMBF16.swift:208-264) and, for e4m3, the
  * widened route (WeightProducts.swift:995-1001 -> GEMM.linear, GEMM.swift:297-345).
- * Dispatches on the weight's kind and on m: m <= 4 runs the GEMV, 4 < m <= 32 the skinny
- * tensor-core product (K split over a cluster), larger m the tensor-core GEMMs.  x, y, bias: device pointers, 16-byte aligned; K a multiple of 8.
+ * Dispatches on the weight's kind and on m: m <= 4 runs the GEMV (an int8 weight of 3 or 4 rows given the
+ * workspace sc_workspace_size reports: the integer skinny product), 4 < m <= 32 the skinny tensor-core
+ * products, larger m the tensor-core GEMMs.  x, y, bias: device pointers, 16-byte aligned; K a multiple of 8.
  * workspace may be NULL when sc_workspace_size reports 0 (and from 1536 rows, at the cost of speed).
  */
 SC_API sc_status sc_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t m, const sc_bf16* bias, sc_bf16* y,

@@ -260,7 +260,12 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
   if ((s = enter(ctx)) != SC_OK) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((s = rotate_operand(ctx, w, x, m, workspace, workspace_bytes, st)) != SC_OK) return s;
-  if (m <= kSkinnyMinRows) return run_gemv(ctx, w, x, m, bias, y, f32_out, workspace, workspace_bytes, st);
+  // int8 products of kSkinnyI8MinRows < m <= kSkinnyMinRows go to the integer skinny product when its
+  // workspace is there (it reads the weight once whatever m is, where the GEMV's arithmetic grows with m)
+  const bool i8_small = m > kSkinnyI8MinRows && m <= kSkinnyMinRows && skinny_i8_grid(w, m, ctx->sm_count) > 0 &&
+                        workspace != nullptr;
+  if (m <= kSkinnyMinRows && !i8_small)
+    return run_gemv(ctx, w, x, m, bias, y, f32_out, workspace, workspace_bytes, st);
   CUtensorMap tmx;
   if (m <= 32) {
     if ((s = make_tmap_x(ctx, x, m, w->k, &tmx, gemm_skinny_box_rows(m))) != SC_OK) return s;
@@ -281,6 +286,7 @@ sc_status run_linear(sc_ctx* ctx, const sc_weight* w, const sc_bf16* x, int64_t 
         return s;
       return counters_launched(ctx, ctx->skinny_guard, st);
     }
+    if (i8_small) return run_gemv(ctx, w, x, m, bias, y, f32_out, workspace, workspace_bytes, st);
     return check_cuda(ctx, launch_gemm_skinny(tmx, w, bias, y, f32_out, m, ctx->d_err, ctx->sm_count, st),
                       "skinny gemm launch");
   }
@@ -709,7 +715,9 @@ sc_status sc_rotate_activation(sc_ctx* ctx, const sc_bf16* x, int64_t m, int64_t
 sc_status sc_workspace_size(sc_ctx* ctx, const sc_weight* w, int64_t m, size_t* bytes) {
   if (ctx == nullptr) return SC_INVALID_ARG;
   if (w == nullptr || bytes == nullptr || m < 0) return fail(ctx, SC_INVALID_ARG, "bad argument");
-  if (m > kSkinnyMinRows && m <= 32) {
+  if (m > kSkinnyI8MinRows && m <= kSkinnyMinRows && skinny_i8_grid(w, m, ctx->sm_count) > 0) {
+    *bytes = skinny_i8_workspace_bytes(w, m, skinny_i8_grid(w, m, ctx->sm_count));
+  } else if (m > kSkinnyMinRows && m <= 32) {
     const int grid = skinny_i8_grid(w, m, ctx->sm_count);
     *bytes = grid > 0 ? skinny_i8_workspace_bytes(w, m, grid) : 0;
   } else if (m >= 1 && m <= 32) {

@@ -205,6 +205,8 @@ cudaError_t launch_gemm_skinny(const CUtensorMap& tmap_x, const sc_weight* w, co
                                bool f32_out, int64_t m, int* err, int sm_count, cudaStream_t stream);
 // Rows above which sc_linear leaves the GEMV for the skinny tensor-core product.
 constexpr int64_t kSkinnyMinRows = 4;
+// Rows above which an int8 product given the workspace takes the integer skinny product (below: the GEMV).
+constexpr int64_t kSkinnyI8MinRows = 2;
 // The int8 skinny product on the integer tensor cores (sc_gemm_skinny_sk.cu): x written as three exact 8-bit
 // digit planes, the codes multiplied as stored, the work split in equal shares over one CTA per SM, for
 // 4 < m <= kSkinnyI8MaxRows (above that the planes' share of the operand traffic makes the cluster kernel

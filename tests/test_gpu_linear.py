@@ -252,9 +252,11 @@ def test_skinny_tensor_core_product_agrees_with_gemv(ctx, kind, m, nan):
     w.close()
 
 
-@pytest.mark.parametrize("m,k,n", [(16, 4096, 12288), (12, 12288, 4096), (7, 2048, 8000), (9, 512, 38400), (13, 3000, 3200)])
+@pytest.mark.parametrize("m,k,n", [(16, 4096, 12288), (12, 12288, 4096), (7, 2048, 8000), (9, 512, 38400), (13, 3000, 3200),
+                                   (3, 4096, 12288), (4, 2048, 8000)])
 def test_int8_skinny_product_matches_the_oracle_and_repeats(ctx, m, k, n):
-    """With its workspace, an int8 product of 4 < m <= 16 rows runs on the integer tensor cores: x as three
+    """With its workspace, an int8 product of 2 < m <= 16 rows runs on the integer tensor cores (without it,
+    3 or 4 rows run the GEMV): x as three
     exact 8-bit digit planes, the codes as stored, the weight split in equal shares over one CTA per SM (with
     K = 512 a tile is two units and a share four or five: partials meet through the fix-up).  fp32 output
     within the oracle's bar (the integer sum is exact where the oracle's fp32 sum rounds), the same bits on a
