@@ -101,6 +101,39 @@ __device__ __forceinline__ float epi_value(uint32_t raw, float sc, float bi, flo
   return __fadd_rn(__fmul_rn(__uint_as_float(raw), sc), bi);
 }
 
+// Narrow pieces.  When a product's 256 x 256 tiles would leave most pairs idle and their epilogues carry the
+// work that bounds it (the column-parallel gather at 8 GPUs: a rank's 4096 x 384 columns are 24 tiles for 74
+// pairs, and each tile is stored to every rank), the output is cut into pieces of 256 rows x `width` columns,
+// `per_row` of them per row tile, one per pair, so that more SMs share the stores.  A piece is one pair MMA of
+// N = width over the full K: every output is the same sum in the same K order, the same bits as in the whole
+// tile.  The weight's box stays 128 rows a CTA (the rows past the piece are loaded and not used).  width 0:
+// tiles.
+struct Pieces {
+  int width;
+  int per_row;
+  int count;
+};
+
+// The work of the pair at `tile` (tile = pair + j pairs): its row tile, first column and width (false when
+// the pair has no more work).  Only the gathering kernels (kPieces) take pieces.
+template <bool kPieces>
+__device__ __forceinline__ bool job_of(int tile, int num_tiles, int m_tiles, int n_tiles, const Pieces& pc, int& mt,
+                                       int& n0, int& w) {
+  if (!kPieces || pc.width == 0) {
+    if (tile >= num_tiles) return false;
+    int nt;
+    tile_coords(tile, m_tiles, n_tiles, mt, nt);
+    n0 = nt * BN;
+    w = BN;
+    return true;
+  }
+  if (tile >= pc.count) return false;
+  mt = tile / pc.per_row;
+  n0 = (tile % pc.per_row) * pc.width;
+  w = pc.width;
+  return true;
+}
+
 // kI8: both operands int8 codes (x's per-row codes, the weight's codes made signed), 128 codes = 128
 // bytes per K stage, tcgen05.mma kind::i8 into s32 accumulators; row_scales holds s_x per row.
 // kFW (fused widening, 1 int8 / 2 e4m3 / 3 e4m3 with NaN codes): the CTAs widen the codes themselves.
@@ -116,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    int M, int N, int k_tiles, int m_tiles, int n_tiles, int* err,
                    const __grid_constant__ PeerOut peers, const float* __restrict__ gate,
                    const float* __restrict__ row_scales, const __grid_constant__ HeadOut ho, const XHeads xh,
-                   const __grid_constant__ FusedWiden fw) {
+                   const __grid_constant__ FusedWiden fw, const Pieces pc) {
   static_assert(kOp != kOpResidual || kF32Out, "the residual is fp32");
   static_assert(kOp != kOpGelu || !kF32Out, "the GELU output is bf16");
   static_assert(!kI8 || (kOp == kOpNone && !kPeers), "W8A8 stores plain outputs");
@@ -190,11 +223,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0, ready_block = -1;
       uint32_t phase = 0, issued = 0, last_parity = 0;
-      for (int tile = pair; tile < num_tiles && !*abort; tile += pairs) {
-        int mt, nt;
-        tile_coords(tile, m_tiles, n_tiles, mt, nt);
+      for (int tile = pair; !*abort; tile += pairs) {
+        int mt, n0, wd;
+        if (!job_of<kPeers>(tile, num_tiles, m_tiles, n_tiles, pc, mt, n0, wd)) break;
         const int row0 = mt * 2 * BM + static_cast<int>(rank) * BM;
-        const int col0 = nt * BN + static_cast<int>(rank) * BNH;
+        const int col0 = n0 + static_cast<int>(rank) * (wd / 2);
+        const int nt = n0 / BN;  // kFW products have no pieces: the job is the tile of column block nt
         if (kFW != 0 && nt != ready_block) {
           // the tile's column block widened by every CTA (bounded wait)
           const unsigned long long t0 = global_ns();
@@ -235,11 +269,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA) ----------------
     if (leader && lane == 0) {
-      const uint32_t idesc = kI8 ? umma_idesc_s8(2 * BM, BN) : umma_idesc_bf16(2 * BM, BN);
+      const uint32_t idesc_full = kI8 ? umma_idesc_s8(2 * BM, BN) : umma_idesc_bf16(2 * BM, BN);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += pairs) {
+      for (int tile = pair; ok; tile += pairs) {
+        int mt_, n0_, wd;
+        if (!job_of<kPeers>(tile, num_tiles, m_tiles, n_tiles, pc, mt_, n0_, wd)) break;
+        const uint32_t idesc = !kPeers || wd == BN ? idesc_full : umma_idesc_bf16(2 * BM, wd);
         if (!mbar_wait(&s.acc_empty[acc], acc_phase ^ 1u, abort, err, kSiteMmaAccum)) break;
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(acc * BN);
@@ -313,14 +350,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     const bool vec_ok = (N % 8) == 0, vec4_ok = (N % 4) == 0;
     const bool has_bias = bias != nullptr;
-    for (int tile = pair; tile < num_tiles; tile += pairs) {
-      int mt, nt;
-      tile_coords(tile, m_tiles, n_tiles, mt, nt);
-      const int n0 = nt * BN;
+    for (int tile = pair;; tile += pairs) {
+      int mt, n0, wd;
+      if (!job_of<kPeers>(tile, num_tiles, m_tiles, n_tiles, pc, mt, n0, wd)) break;
       const int row = mt * 2 * BM + static_cast<int>(rank) * BM + ew * 32 + lane;
       const float sxr = kI8 && row < M ? row_scales[row] : 0.0f;
       __syncwarp();
-      for (int c = lane; c < BN; c += 32) {
+      for (int c = lane; c < wd; c += 32) {
         const int n = n0 + c;
         s_scale[c] = scales[n];
         s_bias[c] = (bias != nullptr && n < N) ? __uint_as_float(static_cast<uint32_t>(bias[n]) << 16) : 0.0f;
@@ -476,9 +512,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
 #pragma unroll 1
-      for (int ch = 0; ch < (kOp == kOpQkRope || kOp == kOpSwiglu ? 0 : BN / 32); ++ch) {
+      for (int ch = 0; ch < (kOp == kOpQkRope || kOp == kOpSwiglu ? 0 : wd / 32); ++ch) {
         float4 xnext[8];
-        if (kOp == kOpResidual && res_fast && ch + 1 < BN / 32) {
+        if (kOp == kOpResidual && res_fast && ch + 1 < wd / 32) {
 #pragma unroll
           for (int it = 0; it < 8; ++it) {
             const int grow = row0 + ((it * 32 + lane) >> 3);
@@ -717,7 +753,15 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
     }
     if (resident[dev & 63] < max_pairs) max_pairs = resident[dev & 63];
   }
-  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  // Pieces of 128 columns (Pieces) for the gathering product when its tiles fill under half the pairs and the
+  // pieces still fit them.
+  Pieces pc{0, 0, 0};
+  if (kPeers && !kI8 && xh.tokens == 0 && 2 * tiles <= max_pairs) {
+    const int per_row = static_cast<int>((w->n + 127) / 128);
+    if (m_tiles * per_row <= max_pairs && m_tiles * per_row > tiles) pc = Pieces{128, per_row, m_tiles * per_row};
+  }
+  const int jobs = pc.width != 0 ? pc.count : tiles;
+  const int pairs = jobs < max_pairs ? jobs : max_pairs;
   if (kFW != 0) {
     // One group of the tile order (m_tiles <= 16): tile t has column block t / m_tiles, so the first round
     // (tiles 0 .. pairs - 1) reads blocks 0 .. (pairs - 1) / m_tiles.
@@ -754,7 +798,7 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
       cfg.numAttrs = 3;
       const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias,
                                                y, static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles,
-                                               n_tiles, err, peers, gate, row_scales, ho, xh, fw);
+                                               n_tiles, err, peers, gate, row_scales, ho, xh, fw, pc);
       if (e == cudaSuccess) {
         cooperative[dev & 63] = 1;
         return e;
@@ -767,7 +811,7 @@ cudaError_t launch_gemm(const CUtensorMap& tm_x, const CUtensorMap& tm_w, const 
   }
   return cudaLaunchKernelEx(&cfg, kernel, tm_x, tm_w, static_cast<const float*>(w->scales), bias, y,
                             static_cast<int>(m), static_cast<int>(w->n), k_tiles, m_tiles, n_tiles, err, peers, gate,
-                            row_scales, ho, xh, fw);
+                            row_scales, ho, xh, fw, pc);
 }
 
 // The weight's arena codes (int8 stored biased by 128) made signed again for the int8 MMA: code ^ 0x80.
